@@ -1,0 +1,215 @@
+"""Generate the golden fixtures in this directory from the REFERENCE's own oracles.
+
+Run once, in a container where the AnimaXS source tree is present:
+
+    python tests/golden/make_golden.py --reference <path-to-AnimaXS-checkout>
+
+It imports the reference's PyTorch CPU oracles
+(``scripts/dit_source_oracle.py`` and ``scripts/qwen_comfy_oracle.py``) and
+calls their functions -- ``rms_norm``, ``dit_rope``, ``apply_split_half_rope``,
+``scaled_dot_product``, ``precompute_freqs_cis``, ``apply_rope``,
+``attention_pytorch`` -- on seeded inputs, then writes small ``.npz`` files:
+
+* ``rope_tables.npz``   -- sampled rows + full-table checksums of the 3-D RoPE
+  tables for the 32x32 / 64x64 / 128x128 grids, the reference's committed
+  ``scripts/oracle_out/dit_rope_oracle.npz`` (sampled rows), and the Qwen
+  1-D table (theta 1e6).
+* ``attn_small.npz``    -- complete outputs of small cases (DiT self with
+  rms+rope3d, DiT cross with rms and with/without a key-padding mask, Qwen
+  GQA prefill with causal + padding masks).
+* ``attn_configs.npz``  -- outputs at sampled query rows for the benchmark
+  configurations 1, 2, 3 (layers 0 and 27), 4 (a subset of blocks) and 5.
+
+Only the inputs' seeds are stored (plus checksums of the inputs to detect a
+change in ``torch.Generator``); tests regenerate inputs with
+``oracle/inputs.py``.  Nothing here is imported at test time -- the tests
+read the ``.npz`` files only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle import inputs  # noqa: E402  (seeded input generator only)
+
+SAMPLE_ROWS = [0, 1, 2, 3, 5, 8, 31, 63, 64, 127, 128, 129, 200, 255, 256, 298, 299,
+               300, 301, 383, 384, 511, 512, 1000, 1023, 1024, 2047, 2048, 3000, 4095,
+               4096, 8191, 8192, 12345, 16383]
+
+
+def sample_rows(n: int) -> np.ndarray:
+    return np.array(sorted({r for r in SAMPLE_ROWS if r < n}), dtype=np.int64)
+
+
+def checksum(x) -> np.ndarray:
+    x = np.asarray(x, dtype=np.float64)
+    return np.array([x.sum(), np.abs(x).sum(), (x * x).sum()], dtype=np.float64)
+
+
+def load_reference(path: str):
+    sys.path.insert(0, os.path.join(path, "scripts"))
+    import dit_source_oracle as dso  # noqa: E402
+    import qwen_comfy_oracle as qco  # noqa: E402
+    return dso, qco
+
+
+def t32(x):
+    return torch.from_numpy(np.asarray(x, dtype=np.float32))
+
+
+def ref_dit(dso, case, rows):
+    """DiT path: rms_norm -> (apply_split_half_rope) -> scaled_dot_product, fp32."""
+    q, k, v = t32(case.q), t32(case.k), t32(case.v)
+    ones = torch.ones(128, dtype=torch.float32)
+    qn, kn = dso.rms_norm(q, ones), dso.rms_norm(k, ones)
+    if case.qk_norm == "rms_rope":
+        qn, kn = dso.apply_split_half_rope(qn, kn, t32(case.rope_table))
+    if case.kv_valid_len is None:
+        outs = []
+        for h in range(q.shape[2]):  # per head: scaled_dot_product holds all scores
+            outs.append(dso.scaled_dot_product(qn[:, rows, h:h + 1], kn[:, :, h:h + 1],
+                                               v[:, :, h:h + 1]))
+        return torch.cat(outs, dim=2).numpy()
+    return ref_masked(case, qn, kn, v, rows, causal=False)
+
+
+def ref_masked(case, qn, kn, v, rows, causal):
+    """Masked SDPA through the reference's attention_pytorch (additive mask)."""
+    _, qco = REF
+    b, sq, hq, d = qn.shape
+    sk, hkv = kn.shape[1], kn.shape[2]
+    valid = case.kv_valid_len[0] if case.kv_valid_len else sk
+    # QwenOracle.forward mask construction (qwen_comfy_oracle.py:238-248)
+    am = torch.zeros(1, sk)
+    am[:, :valid] = 1.0
+    mask = 1.0 - am.reshape(1, 1, -1, sk).expand(1, 1, sq, sk)
+    mask = mask.masked_fill(mask.to(torch.bool), torch.finfo(torch.float32).min / 4)
+    if causal:
+        cm = torch.empty(sq, sk).fill_(torch.finfo(torch.float32).min / 4).triu_(1)
+        mask = mask + cm
+    mask = mask[:, :, rows, :].reshape(1, len(rows), sk)
+    xq = qn[:, rows].transpose(1, 2)
+    xk = kn.transpose(1, 2)
+    xv = v.transpose(1, 2)
+    out = qco.attention_pytorch(xq, xk, xv, hq, mask=mask, skip_reshape=True,
+                                enable_gqa=(hq != hkv))
+    return out.reshape(b, len(rows), hq, d).numpy()
+
+
+def ref_qwen(case, rows):
+    """Qwen path: rms_norm -> precompute_freqs_cis/apply_rope -> attention_pytorch."""
+    _, qco = REF
+    q, k, v = t32(case.q), t32(case.k), t32(case.v)
+    s = q.shape[1]
+    ones = torch.ones(128, dtype=torch.float32)
+    xq = qco.rms_norm(q.transpose(1, 2), ones, 1e-6)
+    xk = qco.rms_norm(k.transpose(1, 2), ones, 1e-6)
+    pos = torch.arange(0, s).unsqueeze(0)
+    freqs = qco.precompute_freqs_cis(128, pos, 1.0e6)
+    xq, xk = qco.apply_rope(xq, xk, freqs)
+    return ref_masked(case, xq.transpose(1, 2), xk.transpose(1, 2), v, rows, causal=True)
+
+
+def main():
+    global REF
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="AnimaXS source checkout")
+    ap.add_argument("--skip-large", action="store_true")
+    args = ap.parse_args()
+    REF = load_reference(args.reference)
+    dso, qco = REF
+    torch.set_num_threads(os.cpu_count())
+
+    # ---------------- RoPE tables ----------------
+    rope = {}
+    for (t, h, w) in [(1, 32, 32), (1, 64, 64), (1, 128, 128)]:
+        tab = dso.dit_rope(h, w, t).numpy()
+        rows = sample_rows(tab.shape[0])
+        key = f"rope3d_{t}x{h}x{w}"
+        rope[key + "_rows"] = rows
+        rope[key + "_sample"] = tab[rows]
+        rope[key + "_checksum"] = checksum(tab)
+    committed = np.load(os.path.join(args.reference, "scripts/oracle_out/dit_rope_oracle.npz"))
+    rows = sample_rows(committed["rope"].shape[0])
+    rope["committed_rope_rows"] = rows
+    rope["committed_rope_sample"] = committed["rope"][rows]
+    rope["committed_rope_checksum"] = checksum(committed["rope"])
+    cos, sin, nsin = qco.precompute_freqs_cis(128, torch.arange(0, 512).unsqueeze(0), 1.0e6)
+    cos = cos.reshape(512, 128).numpy()
+    sin = sin.reshape(512, 64).numpy()
+    nsin = nsin.reshape(512, 64).numpy()
+    rows = sample_rows(512)
+    rope["rope1d_512_rows"] = rows
+    rope["rope1d_512_cos"] = cos[rows, :64]
+    rope["rope1d_512_sin"] = sin[rows]
+    rope["rope1d_512_nsin"] = nsin[rows]
+    rope["rope1d_512_checksum"] = checksum(np.concatenate([cos[:, :64], sin], axis=1))
+    np.savez_compressed(os.path.join(HERE, "rope_tables.npz"), **rope)
+
+    # ---------------- small complete cases ----------------
+    small = {}
+
+    def add(name, case, out, seed_info):
+        small[name + "_out"] = out.astype(np.float32)
+        small[name + "_in_checksum"] = np.concatenate([checksum(case.q), checksum(case.k),
+                                                       checksum(case.v)])
+        small[name + "_meta"] = np.array(seed_info, dtype=np.int64)
+
+    c = inputs.dit_self(seed=10, grid=(1, 16, 16), heads=2)
+    add("dit_self_256", c, ref_dit(dso, c, np.arange(256)), [10, 1, 16, 16, 2])
+    c = inputs.dit_cross(seed=11, q_len=192, kv_len=96, heads=2, kv_valid=40)
+    add("dit_cross_192x96_valid40", c, ref_dit(dso, c, np.arange(192)), [11, 192, 96, 2, 40])
+    c = inputs.dit_cross(seed=12, q_len=130, kv_len=200, heads=2, kv_valid=None)
+    add("dit_cross_130x200", c, ref_dit(dso, c, np.arange(130)), [12, 130, 200, 2, 0])
+    c = inputs.qwen_prefill(layer=0, seq_len=160, heads=4, kv_heads=2, valid=100)
+    add("qwen_160_h4kv2_valid100", c, ref_qwen(c, np.arange(160)), [0, 160, 4, 2, 100])
+    np.savez_compressed(os.path.join(HERE, "attn_small.npz"), **small)
+
+    if args.skip_large:
+        return
+    # ---------------- benchmark configurations at sampled rows ----------------
+    big = {}
+
+    def addbig(name, case, out, rows):
+        big[name + "_rows"] = rows
+        big[name + "_out"] = out.astype(np.float32)
+        big[name + "_in_checksum"] = np.concatenate([checksum(case.q), checksum(case.k),
+                                                     checksum(case.v)])
+
+    c = inputs.dit_self(seed=0, grid=(1, 32, 32))
+    rows = sample_rows(1024)
+    addbig("cfg1", c, ref_dit(dso, c, rows), rows)
+    c = inputs.dit_cross(seed=0)
+    rows = sample_rows(4096)
+    addbig("cfg2_masked", c, ref_dit(dso, c, rows), rows)
+    c.kv_valid_len = None
+    addbig("cfg2_unmasked", c, ref_dit(dso, c, rows), rows)
+    for layer in (0, 27):
+        c = inputs.qwen_prefill(layer=layer)
+        rows = sample_rows(512)
+        addbig(f"cfg3_l{layer}", c, ref_qwen(c, rows), rows)
+    for prompt in (0, 7):
+        for step in (0, 7):
+            for block in (0, 27):
+                sc, cc = inputs.workload_block(prompt, step, block)
+                rows = sample_rows(4096)[::3]
+                tag = f"cfg4_p{prompt}_s{step}_b{block}"
+                addbig(tag + "_self", sc, ref_dit(dso, sc, rows), rows)
+                addbig(tag + "_cross", cc, ref_dit(dso, cc, rows), rows)
+    c = inputs.dit_self(seed=0, grid=(1, 128, 128))
+    rows = sample_rows(16384)
+    addbig("cfg5", c, ref_dit(dso, c, rows), rows)
+    np.savez_compressed(os.path.join(HERE, "attn_configs.npz"), **big)
+
+
+REF = None
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,150 @@
+"""Pin the CPU oracle (oracle/attn_oracle.py) against fixtures produced by the
+reference's own PyTorch oracles (tests/golden/make_golden.py) and against the
+reference's Swift known-answer tests (DitRoPETests, DiTBlockTests,
+GqaHeadMappingTests)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import attn_oracle as ora
+from oracle import inputs
+from tests.conftest import GOLDEN
+
+
+def _npz(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def _checksum(x):
+    x = np.asarray(x, dtype=np.float64)
+    return np.array([x.sum(), np.abs(x).sum(), (x * x).sum()])
+
+
+@pytest.mark.parametrize("grid", [(1, 32, 32), (1, 64, 64), (1, 128, 128)])
+def test_rope3d_table_matches_reference(grid):
+    g = _npz("rope_tables.npz")
+    key = "rope3d_{}x{}x{}".format(*grid)
+    tab = ora.dit_rope_table(*grid)
+    rows = g[key + "_rows"]
+    np.testing.assert_allclose(tab[rows], g[key + "_sample"], atol=2e-6, rtol=0)
+    np.testing.assert_allclose(_checksum(tab), g[key + "_checksum"], rtol=1e-6)
+
+
+def test_rope3d_matches_reference_committed_golden():
+    # scripts/oracle_out/dit_rope_oracle.npz (the reference's own fixture)
+    g = _npz("rope_tables.npz")
+    tab = ora.dit_rope_table(1, 32, 32)
+    np.testing.assert_allclose(tab[g["committed_rope_rows"]], g["committed_rope_sample"], atol=2e-6)
+    np.testing.assert_allclose(_checksum(tab), g["committed_rope_checksum"], rtol=1e-6)
+
+
+def test_rope1d_matches_reference():
+    g = _npz("rope_tables.npz")
+    tab = ora.rope1d_table(512, 1.0e6)
+    rows = g["rope1d_512_rows"]
+    # Angles reach 511 rad, where one fp32 ulp of the inverse frequency (torch's
+    # pow vs libm powf, which the Swift makeRope uses) moves cos/sin by ~3e-5.
+    tol = 4e-5
+    np.testing.assert_allclose(tab[rows, :, 0, 0], g["rope1d_512_cos"], atol=tol)
+    np.testing.assert_allclose(tab[rows, :, 1, 0], g["rope1d_512_sin"], atol=tol)
+    # precompute_freqs_cis returns -sin for the second half; the table stores it at [0,1]
+    np.testing.assert_allclose(tab[rows, :, 0, 1], g["rope1d_512_nsin"], atol=tol)
+
+
+def test_rope3d_known_answers():
+    # DitRoPETests.swift: token 0 is the identity; w=1 / w=17 anchors; t,h,w order.
+    tab = ora.dit_rope_table(1, 32, 32)
+    np.testing.assert_allclose(tab[0].reshape(64, 4), np.tile([1, 0, 0, 1], (64, 1)), atol=1e-7)
+    np.testing.assert_allclose(tab[1, 43].ravel(), [np.cos(1.0), -np.sin(1.0), np.sin(1.0), np.cos(1.0)], atol=1e-6)
+    np.testing.assert_allclose(tab[17, 43].ravel(), [np.cos(17.0), -np.sin(17.0), np.sin(17.0), np.cos(17.0)], atol=1e-5)
+    # h=1 (token 32): first height pair (index 22) rotates by 1 rad, width pairs are identity
+    np.testing.assert_allclose(tab[32, 22].ravel(), [np.cos(1.0), -np.sin(1.0), np.sin(1.0), np.cos(1.0)], atol=1e-6)
+    np.testing.assert_allclose(tab[32, 43:].reshape(-1, 4), np.tile([1, 0, 0, 1], (21, 1)), atol=1e-7)
+    # thetas (DitRoPETests.swift:114-120)
+    assert abs(float(np.float32(10000.0 * 4.0 ** (42 / 40))) - 42870.938501451725) < 0.01
+
+
+def test_split_half_pairing_known_answers():
+    # DiTBlockTests.swift:18-65: pairs (p, p+D/2), not adjacent.
+    x = np.array([1, 2, 3, 4], np.float32).reshape(1, 1, 1, 4)
+    table = np.zeros((1, 2, 2, 2), np.float32)
+    table[0, 0] = [[0, -1], [1, 0]]     # 90 degrees
+    table[0, 1] = [[-1, 0], [0, -1]]    # 180 degrees
+    out = ora.apply_split_half_rope(x, table).ravel()
+    np.testing.assert_allclose(out, [-3, -2, 1, -4], atol=1e-6)
+    x8 = np.array([1, 2, 3, 4, 10, 20, 30, 40], np.float32).reshape(1, 1, 1, 8)
+    ident = np.zeros((1, 4, 2, 2), np.float32)
+    ident[0, :, 0, 0] = 1
+    ident[0, :, 1, 1] = 1
+    np.testing.assert_allclose(ora.apply_split_half_rope(x8, ident), x8)
+
+
+def test_gqa_mapping_table():
+    # GqaHeadMappingTests.swift:23-43
+    assert [ora.gqa_kv_head(h, 16, 8) for h in range(16)] == [0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 5, 6, 6, 7, 7]
+    assert [ora.gqa_kv_head(h, 32, 8) for h in (0, 7, 8, 31)] == [0, 1, 2, 7]
+    with pytest.raises(ValueError):
+        ora.gqa_kv_head(0, 6, 4)
+
+
+def test_rms_norm_shared_weight():
+    # DiTBlockTests.swift:89-115: per-head RMSNorm with a shared [D] weight
+    x = np.arange(16, dtype=np.float32).reshape(1, 1, 2, 8) - 5
+    w = np.linspace(0.5, 2, 8).astype(np.float32)
+    out = ora.rms_norm_heads(x, w)
+    for h in range(2):
+        row = x[0, 0, h]
+        np.testing.assert_allclose(out[0, 0, h], row / np.sqrt(np.mean(row * row) + 1e-6) * w, rtol=1e-6)
+
+
+SMALL = {
+    "dit_self_256": lambda: inputs.dit_self(seed=10, grid=(1, 16, 16), heads=2),
+    "dit_cross_192x96_valid40": lambda: inputs.dit_cross(seed=11, q_len=192, kv_len=96, heads=2, kv_valid=40),
+    "dit_cross_130x200": lambda: inputs.dit_cross(seed=12, q_len=130, kv_len=200, heads=2, kv_valid=None),
+    "qwen_160_h4kv2_valid100": lambda: inputs.qwen_prefill(layer=0, seq_len=160, heads=4, kv_heads=2, valid=100),
+}
+
+
+@pytest.mark.parametrize("name", sorted(SMALL))
+def test_oracle_matches_reference_small(name):
+    g = _npz("attn_small.npz")
+    case = SMALL[name]()
+    got_in = np.concatenate([_checksum(case.q), _checksum(case.k), _checksum(case.v)])
+    np.testing.assert_allclose(got_in, g[name + "_in_checksum"], rtol=1e-9)
+    out = case.oracle()
+    np.testing.assert_allclose(out, g[name + "_out"], atol=2e-5, rtol=0)
+
+
+def _cfg_cases():
+    out = {
+        "cfg1": lambda: inputs.dit_self(seed=0, grid=(1, 32, 32)),
+        "cfg2_masked": lambda: inputs.dit_cross(seed=0),
+        "cfg2_unmasked": lambda: inputs.dit_cross(seed=0, kv_valid=None),
+        "cfg3_l0": lambda: inputs.qwen_prefill(layer=0),
+        "cfg3_l27": lambda: inputs.qwen_prefill(layer=27),
+    }
+    for p in (0, 7):
+        for s in (0, 7):
+            for b in (0, 27):
+                tag = f"cfg4_p{p}_s{s}_b{b}"
+                out[tag + "_self"] = (lambda p=p, s=s, b=b: inputs.workload_block(p, s, b)[0])
+                out[tag + "_cross"] = (lambda p=p, s=s, b=b: inputs.workload_block(p, s, b)[1])
+    out["cfg5"] = lambda: inputs.dit_self(seed=0, grid=(1, 128, 128))
+    return out
+
+
+CFG = _cfg_cases()
+FAST_CFG = ["cfg1", "cfg2_masked", "cfg2_unmasked", "cfg3_l0", "cfg3_l27",
+            "cfg4_p0_s0_b0_self", "cfg4_p7_s7_b27_cross", "cfg5"]
+
+
+@pytest.mark.parametrize("name", FAST_CFG)
+def test_oracle_matches_reference_configs(name):
+    g = _npz("attn_configs.npz")
+    case = CFG[name]()
+    rows = g[name + "_rows"]
+    got_in = np.concatenate([_checksum(case.q), _checksum(case.k), _checksum(case.v)])
+    np.testing.assert_allclose(got_in, g[name + "_in_checksum"], rtol=1e-9)
+    out = case.oracle(rows=rows)
+    np.testing.assert_allclose(out, g[name + "_out"], atol=3e-5, rtol=0)
