@@ -1,0 +1,12 @@
+"""animaxs_b200 -- B200 (sm_100a) build of the AnimaXS attention hot path.
+
+The product is ``libanimaxs_attn.so`` (C ABI, ``include/animaxs_attn.h``); this
+package holds its CUDA sources (``csrc/``), the in-tree build
+(``build.py``) and the host-side mirror of the reference's Swift
+``AttentionExecutor`` interface (``executor.py``).
+"""
+
+from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError,  # noqa: F401
+                   AttentionValidationError, LIB_PATH, lib)
+from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  # noqa: F401
+                       DitRoPE, GqaHeadMapping, qwen_rope)

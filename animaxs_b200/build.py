@@ -1,0 +1,79 @@
+"""Build libanimaxs_attn.so in-tree with nvcc for sm_100a (no JIT, no torch extension).
+
+Usage: ``python -m animaxs_b200.build`` (also run by ``__graft_entry__.build()``).
+Objects go to ``animaxs_b200/_build/``; the shared library to
+``animaxs_b200/libanimaxs_attn.so`` so that it travels with the source tree.
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libanimaxs_attn.so")
+SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "qk_norm.cu", "sharded.cu"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
+         "--expt-relaxed-constexpr", "-Xptxas", "-v"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _newer(target: str, deps) -> bool:
+    if not os.path.exists(target):
+        return False
+    t = os.path.getmtime(target)
+    return all(os.path.getmtime(d) <= t for d in deps)
+
+
+def _headers():
+    inc = os.path.join(os.path.dirname(HERE), "include")
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
+    hs += [os.path.join(inc, f) for f in os.listdir(inc) if f.endswith(".h")]
+    return hs
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    cc = nvcc()
+    headers = _headers()
+    objs, jobs = [], []
+    for src in SOURCES:
+        path = os.path.join(CSRC, src)
+        obj = os.path.join(BUILD, src + ".o")
+        objs.append(obj)
+        if force or not _newer(obj, [path] + headers):
+            jobs.append([cc, *ARCH, *FLAGS, "-c", path, "-o", obj])
+    logs = []
+    with cf.ThreadPoolExecutor(max_workers=len(jobs) or 1) as ex:
+        for cmd, res in zip(jobs, ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), jobs)):
+            logs.append((cmd, res))
+            if res.returncode != 0:
+                sys.stderr.write(res.stdout + res.stderr)
+                raise RuntimeError(f"nvcc failed: {' '.join(cmd)}")
+    if verbose:
+        for cmd, res in logs:
+            sys.stderr.write(f"--- {os.path.basename(cmd[-3])}\n{res.stderr}")
+    if force or jobs or not _newer(LIB, objs):
+        link = [cc, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-ldl", "-Xcompiler", "-fPIC"]
+        res = subprocess.run(link, capture_output=True, text=True)
+        if res.returncode != 0:
+            sys.stderr.write(res.stdout + res.stderr)
+            raise RuntimeError("link failed")
+        os.replace(LIB + ".tmp", LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,38 @@
+// api_internal.h -- context layout and helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "../../include/animaxs_attn.h"
+
+struct animaxs_attn_ctx {
+  int device = 0;
+  int num_sms = 0;
+  void* scratch = nullptr;        // normalised q/k copies (grown on demand)
+  size_t scratch_bytes = 0;
+  void* staging = nullptr;        // head-sharded path: per-rank slice + gather buffer
+  size_t staging_bytes = 0;
+  unsigned int* d_status = nullptr;  // device status word written by kernels
+  int64_t query_tiles = 0;
+  std::string last_error;
+};
+
+// Output redirection for the head-sharded path: query head h is written at
+// ptr + (h - head_base) * head.
+struct AxOutView {
+  void* ptr;
+  int64_t tok, head, batch;
+  int head_base;
+};
+
+int ax_set_error(animaxs_attn_ctx* ctx, int code, const char* fmt, ...);
+int ax_cuda_fail(animaxs_attn_ctx* ctx, cudaError_t e, const char* what);
+int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q, const void* k,
+                const void* v, const void* o);
+int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q,
+                     const void* k, const void* v, void* o, int heads_begin, int heads_count,
+                     const AxOutView* o_view, cudaStream_t stream);

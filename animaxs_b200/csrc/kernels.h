@@ -1,0 +1,60 @@
+// kernels.h -- host-side launch interface of the CUDA kernels (internal to the library).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ax {
+
+// Parameters of the flash-attention kernel (attn_fwd_sm100.cu).  q/k/v arrive
+// through TMA tensor maps over [batch][head][token][128] fp16 views (any
+// strides); the output is written with plain stores.
+struct AttnFwdParams {
+  int q_len;
+  int kv_len;
+  int heads_per_kv;      // heads / kv_heads (GQA group size)
+  int kv_valid;          // keys >= kv_valid masked (already clamped to [1, kv_len])
+  const int* kv_valid_dev;  // optional per-batch override (device)
+  int causal;
+  int n_q_tiles;         // ceil(q_len / 128)
+  int head_offset;       // first query head handled by this launch
+  int o_head_base;       // output head index = h - o_head_base
+  float scale_log2;      // softmax scale * log2(e)
+  __half* o;
+  long long o_tok, o_head, o_batch;  // output strides (elements)
+  unsigned int* status;  // device status word (bit 0: a bounded wait timed out)
+};
+
+constexpr unsigned int kStatusTimeoutBit = 1u;  // a bounded device wait expired
+
+constexpr int kTileM = 128;   // query rows per CTA
+constexpr int kTileN = 128;   // keys per K/V tile
+constexpr int kHeadDim = 128;
+
+// One normalisation job: a [batch][tokens][heads][128] fp16 tensor with strides.
+struct NormJob {
+  const __half* in;
+  __half* out;
+  long long in_tok, in_head, in_batch;
+  long long out_tok, out_head, out_batch;
+  int tokens, heads, batch;
+  const __half* weight;  // shared [128] weight or nullptr (ones)
+  long long rows;        // batch * tokens * heads
+};
+
+struct NormParams {
+  NormJob job[2];
+  int njobs;
+  float eps;
+  const float* rope;     // [tokens][64][2][2] or nullptr (no rotation)
+};
+
+cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                            const AttnFwdParams& p, int heads_in_launch, int batch,
+                            cudaStream_t stream);
+
+cudaError_t launch_qk_norm(const NormParams& p, cudaStream_t stream);
+
+}  // namespace ax

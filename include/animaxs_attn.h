@@ -1,0 +1,216 @@
+/*
+ * animaxs_attn.h -- C ABI of libanimaxs_attn.so, the B200 (sm_100a) build of
+ * the AnimaXS attention hot path.
+ *
+ * The reference exposes this path as the Swift class `AttentionExecutor`
+ * (AnimaXS/Runtime/Metal/AttentionExecutor.swift:77-848), the Metal kernels it
+ * and its callers encode (AnimaXS/Shaders/AnimaKernels.metal: rmsnorm_heads_half
+ * :660-689, rms_rope_split_half :696-729, attention_softmax_rows :1051-1100,
+ * dit_flash_attention_h128_q4_k32 :2193-2318), the RoPE table builders
+ * (AnimaXS/Runtime/Text/DitRoPE.swift:58-107,
+ * AnimaXS/Runtime/Metal/QwenEncoderMetal.swift:126-142) and the GQA rule
+ * (AttentionExecutor.swift:222).  Each declaration below names the reference
+ * interface it replaces.  A Swift caller binds this header through a module
+ * map (`module CAnimaxsAttn { header "animaxs_attn.h" link "animaxs_attn" }`).
+ *
+ * Conventions
+ *  - Plain C: pointers, sizes and a descriptor struct; no CUDA or C++ types.
+ *    `stream` arguments are a `cudaStream_t` passed as `void*` (NULL = the
+ *    legacy default stream).
+ *  - Every call returns an `animaxs_status`; nothing aborts.  The message of
+ *    the last failure on a context is returned by animaxs_attn_last_error().
+ *  - Device buffers are fp16 (IEEE half) unless stated; every device pointer
+ *    must be 16-byte aligned and every stride a multiple of 8 elements, which
+ *    the Tensor Memory Accelerator requires (the reference requires 16-byte
+ *    aligned offsets and row stride on its strided path, :799-805).
+ *  - Work is enqueued on `stream` and is asynchronous, like the reference's
+ *    `encode(commandBuffer:...)`.  A context is NOT reentrant: it owns scratch
+ *    memory, exactly like the reference executor's BufferPool (:69-70).  Use one
+ *    context per stream / host thread.
+ */
+#ifndef ANIMAXS_ATTN_H
+#define ANIMAXS_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ANIMAXS_ATTN_ABI_VERSION 1
+
+/* Status codes.  The reference throws AnimapkError.validation(String) for every
+ * argument problem (AttentionExecutor.swift:778-825) and surfaces GPU errors as
+ * `completed.error` (:771); here they are distinct negative codes. */
+typedef enum animaxs_status {
+  ANIMAXS_OK = 0,
+  ANIMAXS_ERR_INVALID_ARG = -1, /* bad shape / offset / causal dims (:784-789) */
+  ANIMAXS_ERR_UNSUPPORTED = -2, /* valid request this build does not run (:157,:174,:687) */
+  ANIMAXS_ERR_OOB = -3,         /* "attention buffer range is out of bounds" (:817-823) */
+  ANIMAXS_ERR_CUDA = -4,        /* CUDA runtime / launch failure */
+  ANIMAXS_ERR_TIMEOUT = -5,     /* a bounded device-side wait expired */
+  ANIMAXS_ERR_NO_DEVICE = -6,   /* no sm_100 device */
+  ANIMAXS_ERR_NCCL = -7,        /* NCCL unavailable or a collective failed */
+  ANIMAXS_ERR_OVERFLOW = -8     /* "attention byte size overflow" (:830-838) */
+} animaxs_status;
+
+/* q/k normalisation fused in front of the attention.
+ *  NONE     - q and k are used as given (AttentionExecutor.encode semantics).
+ *  RMS      - per-(token, head) RMSNorm over head_dim with a shared weight;
+ *             DiT cross-attention (rmsnorm_heads_half, AnimaKernels.metal:660-689,
+ *             called at DiTBlockExecutor.swift:1608-1626).
+ *  RMS_ROPE - RMSNorm then split-half RoPE (pairs p, p+head_dim/2) from a
+ *             [rows, head_dim/2, 2, 2] fp32 table; DiT self-attention and Qwen
+ *             (rms_rope_split_half, AnimaKernels.metal:696-729, called at
+ *             DiTBlockExecutor.swift:1586-1606 and QwenEncoderMetal.swift:329-350). */
+typedef enum animaxs_qk_norm {
+  ANIMAXS_QK_NONE = 0,
+  ANIMAXS_QK_RMS = 1,
+  ANIMAXS_QK_RMS_ROPE = 2
+} animaxs_qk_norm;
+
+/* One attention call.  Replaces the argument list of
+ * AttentionExecutor.encode(commandBuffer:query:queryOffset:key:...:heads:
+ * queryCount:keyCount:headDim:keyValueHeads:causal:probe:layout:)
+ * (AttentionExecutor.swift:122-133).  All strides are in fp16 ELEMENTS.
+ * Token-major DiT tensors ([rows, heads*128]): tok_stride = heads*128,
+ * head_stride = 128.  Head-major tensors ([heads, rows, 128], the Qwen layout):
+ * tok_stride = 128, head_stride = rows*128. */
+typedef struct animaxs_attn_desc {
+  int32_t batch;        /* independent sequences (>= 1) */
+  int32_t heads;        /* query heads, `heads:` */
+  int32_t kv_heads;     /* `keyValueHeads:`; query head h reads kv head h / (heads/kv_heads) */
+  int32_t q_len;        /* `queryCount:` */
+  int32_t kv_len;       /* `keyCount:` */
+  int32_t head_dim;     /* `headDim:`; this build runs 128 */
+  int64_t q_tok_stride, q_head_stride, q_batch_stride;
+  int64_t k_tok_stride, k_head_stride, k_batch_stride;
+  int64_t v_tok_stride, v_head_stride, v_batch_stride;
+  int64_t o_tok_stride, o_head_stride, o_batch_stride;
+  int32_t causal;       /* `causal:`; requires q_len == kv_len (:787); key j visible to row i iff j <= i */
+  int32_t kv_valid_len; /* key padding: keys >= kv_valid_len are masked for every batch;
+                           0 means kv_len (no padding, the reference's semantics) */
+  const int32_t* kv_valid_lens; /* optional DEVICE int32[batch]; overrides kv_valid_len per batch */
+  float scale;          /* softmax scale; 0 means 1/sqrt(head_dim) (:139) */
+  int32_t qk_norm;      /* animaxs_qk_norm */
+  float eps;            /* RMSNorm epsilon; 0 means 1e-6 */
+  const void* q_norm_weight; /* DEVICE fp16[head_dim] shared by all heads, or NULL for ones */
+  const void* k_norm_weight; /* DEVICE fp16[head_dim], or NULL for ones */
+  const float* rope_table;   /* DEVICE fp32[rope_rows][head_dim/2][2][2] blocks [cos,-sin,sin,cos];
+                                row = token index; RMS_ROPE only */
+  int32_t rope_rows;         /* rows in rope_table; must be >= max(q_len, kv_len) */
+  int32_t reserved0;
+  /* Optional extents (bytes from the pointer passed to the call) used for the
+   * reference's range validation (:808-823); 0 = not checked. */
+  int64_t q_bytes, k_bytes, v_bytes, o_bytes;
+} animaxs_attn_desc;
+
+typedef struct animaxs_attn_ctx animaxs_attn_ctx;
+
+/* ABI version of the loaded library (ANIMAXS_ATTN_ABI_VERSION). */
+int animaxs_attn_abi_version(void);
+
+/* Create / destroy an executor context on `device`.  Replaces
+ * AttentionExecutor.init(context:tileRows:numerics:monitor:layout:attentionBackend:)
+ * (AttentionExecutor.swift:97-110); the context owns its scratch like the
+ * reference's BufferPool.  Fails with ANIMAXS_ERR_NO_DEVICE when `device` is
+ * not an sm_100 GPU (there is no CPU fallback). */
+int animaxs_attn_create(int device, animaxs_attn_ctx** out);
+int animaxs_attn_destroy(animaxs_attn_ctx* ctx);
+
+/* Message describing the most recent failure on `ctx` ("" after success). */
+const char* animaxs_attn_last_error(const animaxs_attn_ctx* ctx);
+
+/* Fill `desc` with defaults for a packed token-major call
+ * ([batch, len, heads*128] q/o, [batch, len, kv_heads*128] k/v). */
+int animaxs_attn_desc_init(animaxs_attn_desc* desc, int batch, int heads, int kv_heads,
+                           int q_len, int kv_len, int head_dim);
+
+/* Validate `desc` exactly as animaxs_attn_forward does, without a GPU.
+ * Mirrors AttentionExecutor.validate (AttentionExecutor.swift:778-825). */
+int animaxs_attn_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* desc,
+                          const void* q, const void* k, const void* v, const void* o);
+
+/* Fused attention: (optional q/k RMSNorm [+ split-half RoPE]) -> softmax(q k^T * scale
+ * + masks) v, fp32 accumulation, fp16 output.  Replaces AttentionExecutor.encode
+ * (AttentionExecutor.swift:122-302) together with the rms/rope encodes its
+ * callers issue in front of it (DiTBlockExecutor.swift:1139-1172,
+ * QwenEncoderMetal.swift:264-279).  Asynchronous on `stream`. */
+int animaxs_attn_forward(animaxs_attn_ctx* ctx, const animaxs_attn_desc* desc,
+                         const void* q, const void* k, const void* v, void* o, void* stream);
+
+/* Wait for the work enqueued on `stream` and report device-side failures
+ * (a bounded wait that expired -> ANIMAXS_ERR_TIMEOUT; a CUDA error ->
+ * ANIMAXS_ERR_CUDA).  Replaces the completion half of
+ * AttentionExecutor.execute(...) async throws (AttentionExecutor.swift:751-776),
+ * which awaits the command buffer and rethrows `completed.error`. */
+int animaxs_attn_synchronize(animaxs_attn_ctx* ctx, void* stream);
+
+/* Scratch bytes a call with `desc` needs (the fused q/k normalisation writes
+ * normalised copies).  Replaces maximumScoreScratchBytes(keyCount:queryCount:)
+ * (AttentionExecutor.swift:112-120); the flash kernel itself needs no score scratch. */
+int animaxs_attn_scratch_bytes(const animaxs_attn_desc* desc, int64_t* bytes);
+
+/* Number of (head, 128-row query tile) units executed on this context since
+ * creation; the counter the reference keeps with
+ * MetricsCollector.recordAttentionQueryTile (GenerationMetrics.swift:490-510). */
+int animaxs_attn_query_tiles(const animaxs_attn_ctx* ctx, int64_t* tiles);
+
+/* Standalone per-(token, head) RMSNorm + split-half RoPE, fp16 in/out
+ * ([tokens, heads, head_dim] rows, `row_stride` elements apart per token),
+ * in place allowed.  Replaces kernel rms_rope_split_half
+ * (AnimaKernels.metal:696-729).  `rope_table` is DEVICE fp32
+ * [tokens][head_dim/2][2][2]; `weight` DEVICE fp16[head_dim] or NULL. */
+int animaxs_rms_rope_split_half(animaxs_attn_ctx* ctx, const void* in, void* out,
+                                const void* weight, const float* rope_table,
+                                int tokens, int heads, int head_dim, int64_t row_stride,
+                                float eps, void* stream);
+
+/* Standalone per-(token, head) RMSNorm without RoPE.  Replaces kernel
+ * rmsnorm_heads_half (AnimaKernels.metal:660-689). */
+int animaxs_rmsnorm_heads_half(animaxs_attn_ctx* ctx, const void* in, void* out,
+                               const void* weight, int tokens, int heads, int head_dim,
+                               int64_t row_stride, float eps, void* stream);
+
+/* Host helpers (no GPU).  DiT 3-D RoPE table [T*H*W][64][2][2] fp32 with the
+ * t/h/w = 44/42/42 dim split, theta_hw = 10000*4^(42/40), theta_t = 1e4.
+ * Replaces DitRoPE.generate(T:H:W:) (DitRoPE.swift:58-107).  `out` holds
+ * T*H*W*256 floats. */
+int animaxs_rope3d_table(int T, int H, int W, float* out);
+
+/* 1-D NeoX RoPE table [seq_len][head_dim/2][2][2] fp32, inv_freq =
+ * theta^(-2p/head_dim).  Replaces QwenEncoderMetal.makeRope(tokens:)
+ * (QwenEncoderMetal.swift:126-142, theta 1e6). */
+int animaxs_rope1d_table(int seq_len, int head_dim, double theta, float* out);
+
+/* GQA head map: kv head read by query head `query_head`
+ * (AttentionExecutor.swift:222; GqaHeadMappingTests.swift:17-21).
+ * Returns < 0 (ANIMAXS_ERR_INVALID_ARG) if heads is not a multiple of kv_heads. */
+int animaxs_gqa_kv_head(int query_head, int heads, int kv_heads);
+
+/* ---- Multi-GPU: heads sharded across ranks + one NCCL all-gather ----------
+ * No counterpart exists in the reference (a single-device app); this serves
+ * the 16K-token DiT configuration.  NCCL is loaded at run time (dlopen of
+ * libnccl.so.2), so the library has no link-time NCCL dependency. */
+typedef struct animaxs_comm animaxs_comm;
+
+/* 128-byte NCCL unique id produced on rank 0 and shared by the caller. */
+int animaxs_comm_unique_id(void* id128);
+int animaxs_comm_create(animaxs_attn_ctx* ctx, int world, int rank, const void* id128,
+                        animaxs_comm** out);
+int animaxs_comm_destroy(animaxs_comm* comm);
+
+/* Rank `rank` of `world` computes query heads [rank*heads/world, (rank+1)*heads/world)
+ * of `desc` (q/k/v/o pointers are the FULL tensors, identical on every rank),
+ * then one ncclAllGather assembles every rank's heads into `o`, so every rank
+ * ends with the complete output.  heads must be a multiple of world. */
+int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_comm* comm,
+                                      const animaxs_attn_desc* desc, const void* q,
+                                      const void* k, const void* v, void* o, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANIMAXS_ATTN_H */
