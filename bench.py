@@ -1,0 +1,404 @@
+"""Benchmark: the AnimaXS DiT attention workload (configuration 4) on B200.
+
+One "step" = one image per GPU through the full 8-step DiT attention workload
+at 1024x1024: 8 Euler steps x 28 blocks x (4096-token self-attention with q/k
+RMSNorm + 3-D RoPE (1x64x64), then 4096x512 cross-attention with q/k RMSNorm),
+16 heads x 128.  Images are independent, so N GPUs each process their own
+image per step (weak scaling, no data-path collective).
+
+Printed JSON line (rank 0):
+  value       images/s for the whole job, inputs resident in HBM
+  e2e         the same metric through the C-ABI executor with pinned HOST
+              buffers, host<->device copies inside the timed region
+  roofline    the dominant kernel (the 4096-token self-attention flash kernel),
+              algorithmic FLOPs / its CUDA-event launch duration, vs the
+              measured dense tensor peak
+  cpu_baseline the CPU oracle on a bounded sample (rank 0, N=1)
+
+``--impl reference`` times the reference's own algorithm on the host CPU (the
+numpy restatement of its PyTorch oracles, all host threads) on the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+S_SELF = 4096
+S_CTX = 512
+HEADS = 16
+HD = 128
+BLOCKS = 28
+EULER_STEPS = 8
+CALLS_PER_IMAGE = BLOCKS * EULER_STEPS            # 224 (self, cross) pairs
+SELF_FLOPS = 4.0 * S_SELF * S_SELF * HD * HEADS   # 137.4 GFLOP per self-attention
+CROSS_FLOPS = 4.0 * S_SELF * S_CTX * HD * HEADS   # 17.2 GFLOP per cross-attention
+IMAGE_FLOPS = CALLS_PER_IMAGE * (SELF_FLOPS + CROSS_FLOPS)
+POOL_BLOCKS = 6                                   # distinct resident input sets (> L2)
+
+METRIC = ("DiT attention throughput, 8-step 1024x1024 workload "
+          "(28 blocks x 8 steps x [4096-tok self rms+rope3d + 4096x512 cross rms])")
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d["bf16_tflops_sustained"], d["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU legs --
+def cpu_sample(steps: int = 1):
+    """Time the CPU oracle (numpy, all host threads) on one workload block:
+    the 4096-token self-attention + the 4096x512 cross-attention of
+    (prompt 0, step 0, block 0).  Returns (seconds per block, cores)."""
+    from oracle import inputs  # the checker, used here only as the CPU baseline
+    sc, cc = inputs.workload_block(0, 0, 0)
+    cores = os.cpu_count() or 1
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        sc.oracle()
+        cc.oracle()
+        times.append(time.perf_counter() - t0)
+    return min(times), cores
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    # warm-up then timed, each step one bounded sample (one block of the workload)
+    cpu_sample(max(1, min(args.warmup, 1)))
+    t_block, cores = cpu_sample(args.steps)
+    img_s = 1.0 / (t_block * CALLS_PER_IMAGE)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": img_s, "unit": "img/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_block * CALLS_PER_IMAGE * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU oracle)", "data": "synthetic",
+        "config": {"workload": "config4: 8-step DiT attention @1024^2, 1 image",
+                   "sample": "1 block (self 4096 + cross 4096x512) per step, extrapolated x224"},
+        "tflops": (SELF_FLOPS + CROSS_FLOPS) / t_block / 1e12,
+        "cpu_baseline": {"value": img_s, "unit": "img/s", "cores": cores, "kind": "port",
+                         "sample": "prompt 0 / step 0 / block 0 self+cross, numpy fp32, x224"},
+        "e2e": {"value": img_s, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU legs --
+def make_pool(torch, device, seed):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    pool = []
+    for _ in range(POOL_BLOCKS):
+        def r(*shape):
+            return torch.randn(*shape, generator=g, device=device, dtype=torch.float32).half()
+        pool.append({
+            "sq": r(1, S_SELF, HEADS, HD), "sk": r(1, S_SELF, HEADS, HD), "sv": r(1, S_SELF, HEADS, HD),
+            "cq": r(1, S_SELF, HEADS, HD), "ck": r(1, S_CTX, HEADS, HD), "cv": r(1, S_CTX, HEADS, HD),
+        })
+    return pool
+
+
+def run_gpu(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import animaxs_b200 as ax
+    from oracle import attn_oracle as ora  # RoPE table values only (also built by the C helper)
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ex = ax.AttentionExecutor(local_rank)
+    stream = torch.cuda.current_stream(device)
+    rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).to(device)
+    del ora
+    pool = make_pool(torch, device, 1234 + rank)
+    o_self = torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16, device=device)
+    o_cross = torch.empty_like(o_self)
+    qn = torch.empty_like(o_self)
+    kn = torch.empty_like(o_self)
+
+    ev_pairs = []
+
+    def self_attn(blk, timed):
+        # q/k RMSNorm + 3-D RoPE (two launches), then the flash kernel on the
+        # normalised tensors; events bracket the flash kernel alone.
+        ex.rms_rope_split_half(stream, blk["sq"], qn, None, rope, tokens=S_SELF, heads=HEADS)
+        ex.rms_rope_split_half(stream, blk["sk"], kn, None, rope, tokens=S_SELF, heads=HEADS)
+        if timed:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+        ex.attention(qn, kn, blk["sv"], out=o_self, stream=stream)
+        if timed:
+            b.record(stream)
+            ev_pairs.append((a, b))
+
+    def cross_attn(blk):
+        ex.attention(blk["cq"], blk["ck"], blk["cv"], out=o_cross, qk_norm="rms", stream=stream)
+
+    def image(timed=False):
+        i = 0
+        for _ in range(EULER_STEPS):
+            for _ in range(BLOCKS):
+                blk = pool[i % POOL_BLOCKS]
+                self_attn(blk, timed)
+                cross_attn(blk)
+                i += 1
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        image()
+    barrier()
+    ex.synchronize(stream)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        image(timed=True)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ex.synchronize(stream)
+    elapsed_ms = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(b) for a, b in ev_pairs]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    images = args.steps * world
+    value = images / (elapsed_ms / 1e3)
+    launches = args.steps * CALLS_PER_IMAGE * (3 + 2)   # self: 2 norms + flash; cross: norm + flash
+
+    # ---------------- e2e: fused C-ABI calls with pinned host buffers ----------------
+    e2e = None if args.no_e2e else run_e2e(torch, ex, device, stream, rope, args, world)
+
+    if rank != 0:
+        return
+    peak_burst, peak_sust, hbm, peak_kind = peaks()
+    avg_kern = statistics.mean(kern_ms) if kern_ms else float("nan")
+    achieved = SELF_FLOPS / (avg_kern / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": "config4: 8-step DiT attention @1024^2 (224 self 4096 + 224 cross 4096x512 per image)",
+                   "images_per_gpu_per_step": 1, "global_batch": world, "seq_len": S_SELF,
+                   "ctx_len": S_CTX, "heads": HEADS, "head_dim": HD, "parallelism": f"batch-shard x{world}",
+                   "l2": f"inputs cycled over a {POOL_BLOCKS * 68} MiB resident pool (> 126 MB L2)"},
+        "tflops_per_gpu": IMAGE_FLOPS * args.steps / (elapsed_ms / 1e3) / 1e12,
+        "frac_of_peak_per_gpu": IMAGE_FLOPS * args.steps / (elapsed_ms / 1e3) / 1e12 / peak_sust,
+        "roofline": {"kernel": "attn_fwd_sm100_kernel (4096-token self-attention, 16 heads)",
+                     "bound": "tensor", "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                     "frac": achieved / peak_sust, "peak_kind": f"{peak_kind} bf16 dense, sustained",
+                     "frac_of_burst_peak": achieved / peak_burst,
+                     "flops_per_launch": SELF_FLOPS, "avg_launch_ms": avg_kern,
+                     "traffic": None},
+        "clocks": clocks,
+        "gpu_launches": launches,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        t_block, cores = cpu_sample(1)
+        line["cpu_baseline"] = {"value": 1.0 / (t_block * CALLS_PER_IMAGE), "unit": "img/s",
+                                "cores": cores, "kind": "port",
+                                "sample": "1 block (self 4096 + cross 4096x512), numpy fp32 oracle, x224"}
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(torch, ex, device, stream, rope, args, world):
+    """Same metric through the fused C-ABI call with pinned host inputs/outputs.
+    Per block: H2D of q,k,v (self) + q,k,v (cross), two fused attention calls,
+    D2H of both outputs; copies and compute overlap across three streams."""
+    nblk = 4
+    g = torch.Generator().manual_seed(99)
+    host = []
+    for _ in range(nblk):
+        host.append({k: torch.randn(*(shape), generator=g).half().pin_memory()
+                     for k, shape in (("sq", (1, S_SELF, HEADS, HD)), ("sk", (1, S_SELF, HEADS, HD)),
+                                      ("sv", (1, S_SELF, HEADS, HD)), ("cq", (1, S_SELF, HEADS, HD)),
+                                      ("ck", (1, S_CTX, HEADS, HD)), ("cv", (1, S_CTX, HEADS, HD)))})
+    outs_h = [torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16).pin_memory() for _ in range(4)]
+    dev_in = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host[0].items()}
+              for _ in range(2)]
+    dev_out = [[torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16, device=device) for _ in range(2)]
+               for _ in range(2)]
+    s_in = torch.cuda.Stream(device)
+    s_out = torch.cuda.Stream(device)
+    h2d = sum(v.numel() * 2 for v in host[0].values())
+    d2h = 2 * S_SELF * HEADS * HD * 2
+
+    def one_image():
+        in_ready = [None, None]
+        comp_done = [torch.cuda.Event(), torch.cuda.Event()]
+        out_done = [torch.cuda.Event(), torch.cuda.Event()]
+        first = [True, True]
+        for i in range(CALLS_PER_IMAGE):
+            slot = i & 1
+            src = host[i % nblk]
+            with torch.cuda.stream(s_in):
+                if not first[slot]:
+                    s_in.wait_event(comp_done[slot])
+                for k, v in src.items():
+                    dev_in[slot][k].copy_(v, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+                in_ready[slot] = ev
+            stream.wait_event(in_ready[slot])
+            if not first[slot]:
+                stream.wait_event(out_done[slot])
+            d = dev_in[slot]
+            ex.attention(d["sq"], d["sk"], d["sv"], out=dev_out[slot][0], qk_norm="rms_rope",
+                         rope_table=rope, stream=stream)
+            ex.attention(d["cq"], d["ck"], d["cv"], out=dev_out[slot][1], qk_norm="rms",
+                         stream=stream)
+            comp_done[slot].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done[slot])
+                outs_h[2 * slot].copy_(dev_out[slot][0], non_blocking=True)
+                outs_h[2 * slot + 1].copy_(dev_out[slot][1], non_blocking=True)
+                out_done[slot].record(s_out)
+            first[slot] = False
+
+    steps = max(1, min(args.steps, 2))
+    one_image()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_image()
+    torch.cuda.synchronize(device)
+    el = time.perf_counter() - t0
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([el], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    return {"value": steps * world / el, "unit": "img/s",
+            "h2d_bytes_per_step": h2d * CALLS_PER_IMAGE, "d2h_bytes_per_step": d2h * CALLS_PER_IMAGE,
+            "steps": steps, "path": "AttentionExecutor.attention -> animaxs_attn_forward (fused rms/rope)"}
+
+
+def profile_kernel(args):
+    import torch
+
+    import animaxs_b200 as ax
+    ex = ax.AttentionExecutor(0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    shape = (4, S_SELF, HEADS, HD)
+    q, k, v = (torch.randn(*shape, generator=g, device="cuda").half() for _ in range(3))
+    out = torch.empty_like(q)
+    for _ in range(args.warmup + args.steps):
+        ex.attention(q, k, v, out=out)
+    torch.cuda.synchronize()
+    ex.synchronize()
+    print("profile-kernel done", flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="animaxs", choices=["animaxs", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-kernel", action="store_true",
+                    help="only launch the flash kernel on a batch-4 4096-token self-attention "
+                         "(192 MiB of inputs, > L2): the small case for ncu captures")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.profile_kernel:
+        profile_kernel(args)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
