@@ -161,19 +161,16 @@ def make_pool(torch, device, seed):
 
 
 def run_gpu(args, rank, world, local_rank):
-    import numpy as np
     import torch
     import torch.distributed as dist
 
     import animaxs_b200 as ax
-    from oracle import attn_oracle as ora  # RoPE table values only (also built by the C helper)
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     ex = ax.AttentionExecutor(local_rank)
     stream = torch.cuda.current_stream(device)
     rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).to(device)
-    del ora
     pool = make_pool(torch, device, 1234 + rank)
     o_self = torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16, device=device)
     o_cross = torch.empty_like(o_self)
