@@ -386,7 +386,8 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   p.kv_valid = d->kv_valid_len > 0 ? d->kv_valid_len : d->kv_len;
   p.kv_valid_dev = d->kv_valid_lens;
   p.causal = d->causal ? 1 : 0;
-  p.n_q_tiles = (d->q_len + ax::kTileM - 1) / ax::kTileM;
+  const int rows_per_cta = ax::attn_fwd_rows_per_cta();
+  p.n_q_tiles = (d->q_len + rows_per_cta - 1) / rows_per_cta;
   p.head_offset = heads_begin;
   const float scale = d->scale > 0.f ? d->scale : 1.0f / std::sqrt(static_cast<float>(D));
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -405,7 +406,8 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   p.status = ctx->d_status;
   cudaError_t e = ax::launch_attn_fwd(tq, tk, tv, p, heads_count, d->batch, stream);
   if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "attention launch");
-  ctx->query_tiles += static_cast<int64_t>(heads_count) * d->batch * p.n_q_tiles;
+  ctx->query_tiles += static_cast<int64_t>(heads_count) * d->batch *
+                      ((d->q_len + ax::kTileM - 1) / ax::kTileM);
   return ANIMAXS_OK;
 }
 

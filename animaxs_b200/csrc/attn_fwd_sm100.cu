@@ -5,22 +5,28 @@
 // dit_flash_attention_h128_q4_k32, AnimaKernels.metal:2193-2318, and whose
 // general path is MPS QK^T -> attention_softmax_rows (:1051-1100) -> MPS PV).
 // Same math: O = softmax(Q K^T * scale + mask) V with fp32 softmax statistics,
-// here as an online (flash) softmax over 128-key tiles.
+// computed as an online (flash) softmax over 128-key tiles.
 //
-// One CTA = one 128-row query tile of one (batch, head).  Six warps:
-//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t); reads S from
-//              TMEM, applies causal / key-padding masks, keeps the running
-//              max / sum in fp32, rescales the O accumulator in TMEM, writes
-//              P (fp16) into a 128B-swizzled shared tile, and finally
+// One CTA = two 128-row query tiles (A: rows q0..q0+127, B: q0+128..q0+255) of
+// one (batch, head); both stream the same K/V tiles.  Ten warps:
+//   warps 0-3  softmax for tile A, warps 4-7 softmax for tile B: thread t owns
+//              query row t of its tile (= TMEM lane t).  Per K/V tile it reads
+//              S from TMEM, applies the causal / key-padding masks, updates the
+//              running max (lazily: O is only rescaled when the max grows by
+//              more than 2^8) and sum in fp32, and writes P = exp2(S*c - m) as
+//              fp16 back into TMEM over the consumed S columns.  At the end it
 //              normalises O and stores it.
-//   warp 4     TMA producer: Q once, then K_j / V_j tiles into a 2-stage ring.
-//   warp 5     MMA issuer (one thread) + TMEM owner: S_j = Q K_j^T into one of
-//              two TMEM S buffers, O += P_j V_j into the TMEM O accumulator,
-//              both tcgen05.mma kind::f16 with operands in shared memory.
-// TMEM: columns [0,128) S buffer 0, [128,256) S buffer 1, [256,384) O.
+//   warp 8     MMA issuer + TMEM owner: S_X = Q_X K_j^T (tcgen05.mma kind::f16,
+//              both operands in shared memory) and O_X += P_X V_j with P read
+//              straight from TMEM (A operand in TMEM).
+//   warp 9     TMA producer: both Q tiles once, then K_j / V_j into 2-stage rings.
+// TMEM (512 columns): S_A [0,128), S_B [128,256) (P_X overlays the first 64
+// columns of S_X), O_A [256,384), O_B [384,512).
 //
-// Pipelining: QK^T for tile j+1 runs on the tensor core while the softmax
-// warps work on tile j; PV for tile j is issued as soon as P_j is written.
+// The tensor core alternates PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): while one
+// softmax warpgroup works on its tile, the tensor core runs the other tile's
+// MMAs.  tcgen05.mma ops from one thread execute in issue order, which is what
+// lets QK_X(j+1) overwrite the TMEM columns PV_X(j) reads P_X(j) from.
 #include "kernels.h"
 #include "sm100_ptx.cuh"
 
@@ -29,12 +35,12 @@ namespace {
 
 constexpr uint32_t kTileBytes = kTileM * kHeadDim * 2;  // 32 KiB: one 128x128 fp16 tile
 constexpr uint32_t kPanelBytes = 128 * 128;             // 128 rows x 128 B (64 fp16)
-constexpr uint32_t kSmQ = 0;
-constexpr uint32_t kSmK = kSmQ + kTileBytes;            // 2 stages
+constexpr uint32_t kSmQ = 0;                            // Q_A, Q_B
+constexpr uint32_t kSmK = kSmQ + 2 * kTileBytes;        // 2 stages
 constexpr uint32_t kSmV = kSmK + 2 * kTileBytes;        // 2 stages
-constexpr uint32_t kSmP = kSmV + 2 * kTileBytes;
-constexpr uint32_t kSmBar = kSmP + kTileBytes;
+constexpr uint32_t kSmBar = kSmV + 2 * kTileBytes;
 constexpr uint32_t kSmemBytes = kSmBar + 256 + 1024;    // + barriers + alignment slack
+constexpr int kThreads = 320;
 
 enum : int {
   kBarQ = 0,
@@ -42,21 +48,20 @@ enum : int {
   kBarKEmpty = 3,  // +stage
   kBarVFull = 5,   // +stage
   kBarVEmpty = 7,  // +stage
-  kBarSFull = 9,   // +buffer
-  kBarSFree = 11,  // +buffer
-  kBarPFull = 13,
-  kBarORdy = 14,
+  kBarSFull = 9,   // +tile
+  kBarPFull = 11,  // +tile (128 arrivals)
+  kBarODone = 13,  // +tile
   kBarDone = 15,
   kNumBars = 16
 };
-constexpr uint32_t kSlotTmem = kNumBars * 8;   // byte offset (from kSmBar) of the TMEM address
+constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0;
 constexpr uint32_t kColO = 256;
 constexpr uint32_t kIdescQK = idesc_f16_f32(128, 128, false);  // B = K tile, K-major
 constexpr uint32_t kIdescPV = idesc_f16_f32(128, 128, true);   // B = V tile, MN-major
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled when max grows > 2^8
 
 // K-major operand (rows x 128 fp16 as two 64-column SW128 panels): k-step kk
 // (16 columns) starts in panel kk/4 at byte (kk%4)*32.
@@ -69,12 +74,28 @@ __device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile, int kk) {
   return sw128_desc(tile + kk * 2048, kPanelBytes, 1024);
 }
 
-__device__ __forceinline__ void rescale32(uint32_t (&r)[32], float a) {
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint32_t k_tile) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * a);
+  for (int kk = 0; kk < 8; ++kk)
+    umma_f16_ss(d_tmem, kmajor_desc(q_tile, kk), kmajor_desc(k_tile, kk), kIdescQK,
+                kk > 0 ? 1u : 0u);
+}
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
+                                         bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_f16_ts(d_tmem, p_tmem + kk * 8, vmajor_desc(v_tile, kk), kIdescPV,
+                (accumulate || kk > 0) ? 1u : 0u);
 }
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, int causal) {
+  if (tile_q0 >= q_len) return 0;
+  int e = valid;
+  if (causal) e = min(e, tile_q0 + kTileM);
+  return (e + kTileN - 1) / kTileN;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const AttnFwdParams p) {
@@ -82,7 +103,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t sQ = base + kSmQ, sK = base + kSmK, sV = base + kSmV, sP = base + kSmP;
+  const uint32_t sQ = base + kSmQ, sK = base + kSmK, sV = base + kSmV;
   const uint32_t bar0 = base + kSmBar;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + kSmBar + kSlotTmem);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kSmBar + kSlotAbort);
@@ -90,33 +111,31 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qt = p.causal ? (p.n_q_tiles - 1 - static_cast<int>(blockIdx.x))
-                          : static_cast<int>(blockIdx.x);
+  const int pair = p.causal ? (p.n_q_tiles - 1 - static_cast<int>(blockIdx.x))
+                            : static_cast<int>(blockIdx.x);
   const int h = p.head_offset + static_cast<int>(blockIdx.y);
   const int b = static_cast<int>(blockIdx.z);
   const int kvh = h / p.heads_per_kv;
-  const int q0 = qt * kTileM;
+  const int q0 = pair * 2 * kTileM;
 
   int valid = p.kv_valid;
   if (p.kv_valid_dev != nullptr) valid = p.kv_valid_dev[b];
   valid = min(max(valid, 1), p.kv_len);
-  int kv_end = valid;
-  if (p.causal) kv_end = min(kv_end, q0 + kTileM);
-  const int n_kv = (kv_end + kTileN - 1) / kTileN;
+  const int nA = kv_tiles_for(q0, p.q_len, valid, p.causal);
+  const int nB = kv_tiles_for(q0 + kTileM, p.q_len, valid, p.causal);
+  const int n_kv = max(nA, nB);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) {
-      const uint32_t cnt = (i == kBarSFree || i == kBarSFree + 1 || i == kBarPFull) ? 128u : 1u;
-      mbar_init(BAR(i), cnt);
-    }
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(BAR(i), (i == kBarPFull || i == kBarPFull + 1) ? 128u : 1u);
     *abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == 5) {
+  if (warp == 8) {
     tmem_alloc(bar0 + kSlotTmem, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 9 && lane == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -126,13 +145,15 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 9) {
     // ------------------------------------------------------------ producer --
-    if (lane == 0) {
+    if (lane == 0 && n_kv > 0) {
       int armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
-      mbar_arrive_expect_tx(BAR(kBarQ), kTileBytes);
+      mbar_arrive_expect_tx(BAR(kBarQ), 2 * kTileBytes);
       tma_load_4d(sQ, &tm_q, BAR(kBarQ), 0, q0, h, b);
       tma_load_4d(sQ + kPanelBytes, &tm_q, BAR(kBarQ), 64, q0, h, b);
+      tma_load_4d(sQ + kTileBytes, &tm_q, BAR(kBarQ), 0, q0 + kTileM, h, b);
+      tma_load_4d(sQ + kTileBytes + kPanelBytes, &tm_q, BAR(kBarQ), 64, q0 + kTileM, h, b);
       for (int j = 0; j < n_kv; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -160,41 +181,59 @@ __global__ void __launch_bounds__(192, 1)
         if (armed_v[st]) mbar_wait(BAR(kBarVFull + st), (armed_v[st] - 1) & 1, &local_abort, nullptr);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 8) {
     // ----------------------------------------------------------------- MMA --
-    if (lane == 0) {
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t sQA = sQ, sQB = sQ + kTileBytes;
       bool ok = mbar_wait(BAR(kBarQ), 0, abort_flag, p.status);
+      if (ok) ok = mbar_wait(BAR(kBarKFull + 0), 0, abort_flag, p.status);
       tc_fence_after();
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        if (j < n_kv) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(BAR(kBarKFull + st), ph, abort_flag, p.status)) break;
-          if (!mbar_wait(BAR(kBarSFree + st), ph ^ 1u, abort_flag, p.status)) break;
-          tc_fence_after();
-          const uint32_t d_s = tmem + kColS0 + st * 128;
-          const uint32_t kt = sK + st * kTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ss(d_s, kmajor_desc(sQ, kk), kmajor_desc(kt, kk), kIdescQK, kk > 0 ? 1u : 0u);
-          tc_commit(BAR(kBarSFull + st));
-          tc_commit(BAR(kBarKEmpty + st));
+      if (ok) {
+        if (nA > 0) {
+          issue_qk(tmem + 0, sQA, sK);
+          tc_commit(BAR(kBarSFull + 0));
         }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int st = jj & 1;
-          const uint32_t ph = (jj >> 1) & 1;
-          if (!mbar_wait(BAR(kBarPFull), static_cast<uint32_t>(jj & 1), abort_flag, p.status)) break;
-          if (!mbar_wait(BAR(kBarVFull + st), ph, abort_flag, p.status)) break;
-          tc_fence_after();
-          const uint32_t vt = sV + st * kTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ss(tmem + kColO, kmajor_desc(sP, kk), vmajor_desc(vt, kk), kIdescPV,
-                        (jj > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(BAR(kBarVEmpty + st));
-          tc_commit(BAR(kBarORdy));
+        if (nB > 0) {
+          issue_qk(tmem + 128, sQB, sK);
+          tc_commit(BAR(kBarSFull + 1));
         }
+        tc_commit(BAR(kBarKEmpty + 0));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int j1 = j + 1;
+        const int st1 = j1 & 1;
+        const uint32_t ph1 = (j1 >> 1) & 1;
+        const uint32_t vt = sV + st * kTileBytes;
+        const uint32_t kt1 = sK + st1 * kTileBytes;
+        if (!mbar_wait(BAR(kBarVFull + st), ph, abort_flag, p.status)) break;
+        if (j < nA) {
+          if (!mbar_wait(BAR(kBarPFull + 0), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          tc_fence_after();
+          issue_pv(tmem + kColO, tmem + 0, vt, j > 0);
+          if (j == nA - 1) tc_commit(BAR(kBarODone + 0));
+        }
+        if (j1 < n_kv) {
+          if (!mbar_wait(BAR(kBarKFull + st1), ph1, abort_flag, p.status)) break;
+          tc_fence_after();
+        }
+        if (j1 < nA) {
+          issue_qk(tmem + 0, sQA, kt1);
+          tc_commit(BAR(kBarSFull + 0));
+        }
+        if (j < nB) {
+          if (!mbar_wait(BAR(kBarPFull + 1), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          tc_fence_after();
+          issue_pv(tmem + kColO + 128, tmem + 128, vt, j > 0);
+          if (j == nB - 1) tc_commit(BAR(kBarODone + 1));
+        }
+        if (j1 < nB) {
+          issue_qk(tmem + 128, sQB, kt1);
+          tc_commit(BAR(kBarSFull + 1));
+        }
+        if (j1 < n_kv) tc_commit(BAR(kBarKEmpty + st1));
+        tc_commit(BAR(kBarVEmpty + st));
       }
       // All MMAs this thread issued must retire before TMEM is released.
       tc_commit(BAR(kBarDone));
@@ -203,21 +242,22 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax --
-    const int t = threadIdx.x;  // query row within the tile == TMEM lane
-    const int row = q0 + t;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int X = warp >> 2;              // 0: tile A, 1: tile B
+    const int t = threadIdx.x & 127;      // row within the tile == TMEM lane
+    const int row = q0 + X * kTileM + t;
+    const int nX = X ? nB : nA;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + X * 128;
+    const uint32_t o_addr = tmem + lane_base + kColO + X * 128;
     const float sl2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      ok = mbar_wait(BAR(kBarSFull + sb), ph, abort_flag, p.status);
+    for (int j = 0; j < nX; ++j) {
+      ok = mbar_wait(BAR(kBarSFull + X), static_cast<uint32_t>(j & 1), abort_flag, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t s[4][32];
-      const uint32_t s_addr = tmem + lane_base + kColS0 + sb * 128;
       tmem_ld32(s_addr + 0, s[0]);
       tmem_ld32(s_addr + 32, s[1]);
       tmem_ld32(s_addr + 64, s[2]);
@@ -226,91 +266,86 @@ __global__ void __launch_bounds__(192, 1)
       asm volatile("" : AX_RW32(s[1])::"memory");
       asm volatile("" : AX_RW32(s[2])::"memory");
       asm volatile("" : AX_RW32(s[3])::"memory");
-      tc_fence_before();
-      mbar_arrive(BAR(kBarSFree + sb));
 
       const int key0 = j * kTileN;
-      const bool need_mask = (key0 + kTileN > valid) || (p.causal && key0 + kTileN - 1 > row);
-      float mx = -INFINITY;
+      if ((key0 + kTileN > valid) || (p.causal && key0 + kTileN - 1 > row)) {
+        const int lim = p.causal ? min(valid, row + 1) : valid;  // keys >= lim are masked
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = __uint_as_float(s[c >> 5][c & 31]);
-        if (need_mask) {
-          const int key = key0 + c;
-          if (key >= valid || (p.causal && key > row)) v = -INFINITY;
-        }
-        s[c >> 5][c & 31] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < 128; ++c)
+          if (key0 + c >= lim) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, mx * sl2);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2_approx(m - m_use);
-      float rs = 0.f;
-      uint32_t pk[64];
+      // Row max with 8 independent chains.
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[0][i]);
+#pragma unroll
+      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(s[c >> 5][c & 31]));
+      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+      const float m_new = fmaxf(m, tmax);
+      const bool grow = m_new > m + kRescaleThreshold;  // also true on the first tile
+      const float alpha = grow ? ex2_approx(m - m_new) : 1.f;  // 0 on the first tile (m = -inf)
+      if (grow) {
+        l *= alpha;
+        m = m_new;
+      }
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                       make_float2(0.f, 0.f)};
+      uint32_t pk[2][32];
 #pragma unroll
       for (int c = 0; c < 128; c += 2) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(s[c >> 5][c & 31]), sl2, -m_use));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(s[(c + 1) >> 5][(c + 1) & 31]), sl2, -m_use));
-        rs += p0 + p1;
-        pk[c >> 1] = pack_half2(p0, p1);
+        const float p0 = ex2_approx(fmaf(__uint_as_float(s[c >> 5][c & 31]), sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(s[c >> 5][(c + 1) & 31]), sl2, neg_m));
+        acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], make_float2(p0, p1));
+        pk[c >> 6][(c >> 1) & 31] = pack_half2(p0, p1);
       }
-      l = l * alpha + rs;
-      m = m_new;
-
-      if (j >= 1) {
-        // PV(j-1) must have retired: the O accumulator is stable and P is free.
-        ok = mbar_wait(BAR(kBarORdy), static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
+        // is stable; PV_X(j) is not issued before this thread arrives below.
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t o[32];
-            const uint32_t o_addr = tmem + lane_base + kColO + c4 * 32;
-            tmem_ld32(o_addr, o);
-            tmem_ld_wait(o);
-            rescale32(o, alpha);
-            tmem_st32(o_addr, o);
-          }
-          tmem_st_wait();
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c4 * 32, o);
+          tmem_ld_wait(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_addr + c4 * 32, o);
         }
       }
-      // P row t -> 128B-swizzled K-major tile (two 64-key panels).
-      const uint32_t prow = sP + static_cast<uint32_t>(t) * 128u;
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const uint32_t addr = prow + (ch >> 3) * kPanelBytes + ((((ch & 7) ^ (t & 7))) << 4);
-        st_shared_v4(addr, pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-      }
-      fence_proxy_async_smem();
+      tmem_st32(s_addr + 0, pk[0]);
+      tmem_st32(s_addr + 32, pk[1]);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(BAR(kBarPFull));
+      mbar_arrive(BAR(kBarPFull + X));
+      const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+      const float2 a = add2(a01, a23);
+      l += a.x + a.y;
     }
-    if (ok) {
-      ok = mbar_wait(BAR(kBarORdy), static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status);
+    if (ok && nX > 0) {
+      ok = mbar_wait(BAR(kBarODone + X), 0, abort_flag, p.status);
       ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = 1.f / l;
-      __half* orow = p.o + static_cast<long long>(b) * p.o_batch +
-                     static_cast<long long>(row) * p.o_tok +
-                     static_cast<long long>(h - p.o_head_base) * p.o_head;
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = 1.f / l;
+        __half* orow = p.o + static_cast<long long>(b) * p.o_batch +
+                       static_cast<long long>(row) * p.o_tok +
+                       static_cast<long long>(h - p.o_head_base) * p.o_head;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + kColO + c4 * 32, o);
-        tmem_ld_wait(o);
-        if (row < p.q_len) {
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c4 * 32, o);
+          tmem_ld_wait(o);
+          if (row < p.q_len) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l);
-            v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
-            v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
-            v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(orow + c4 * 32 + i * 8) = v;
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l);
+              v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
+              v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
+              v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + c4 * 32 + i * 8) = v;
+            }
           }
         }
       }
@@ -319,7 +354,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -327,6 +362,8 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 }  // namespace
+
+int attn_fwd_rows_per_cta() { return 2 * kTileM; }
 
 cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const AttnFwdParams& p, int heads_in_launch, int batch,
@@ -339,7 +376,7 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
     configured = true;
   }
   dim3 grid(p.n_q_tiles, heads_in_launch, batch);
-  attn_fwd_sm100_kernel<<<grid, 192, kSmemBytes, stream>>>(tq, tk, tv, p);
+  attn_fwd_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 

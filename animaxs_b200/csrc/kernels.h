@@ -18,7 +18,7 @@ struct AttnFwdParams {
   int kv_valid;          // keys >= kv_valid masked (already clamped to [1, kv_len])
   const int* kv_valid_dev;  // optional per-batch override (device)
   int causal;
-  int n_q_tiles;         // ceil(q_len / 128)
+  int n_q_tiles;         // CTAs along the query axis: ceil(q_len / attn_fwd_rows_per_cta())
   int head_offset;       // first query head handled by this launch
   int o_head_base;       // output head index = h - o_head_base
   float scale_log2;      // softmax scale * log2(e)
@@ -54,6 +54,8 @@ struct NormParams {
 cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const AttnFwdParams& p, int heads_in_launch, int batch,
                             cudaStream_t stream);
+
+int attn_fwd_rows_per_cta();  // query rows one attention CTA covers
 
 cudaError_t launch_qk_norm(const NormParams& p, cudaStream_t stream);
 
