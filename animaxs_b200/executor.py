@@ -106,6 +106,7 @@ class AttentionExecutor:
         rc = self._lib.animaxs_attn_create(self.device, ctypes.byref(ctx))
         raise_for(rc, f"no sm_100 device {device} (animaxs_attn_create -> {rc})")
         self._ctx = ctx
+        self._desc_cache = {}
 
     # -- lifetime ---------------------------------------------------------
     def close(self):
@@ -233,21 +234,31 @@ class AttentionExecutor:
         import torch
         if out is None:
             out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-        b, sq, h, d = q.shape
-        sk, hkv = k.shape[1], k.shape[2]
-        desc = self.make_desc(heads=h, query_count=sq, key_count=sk, head_dim=d,
-                              key_value_heads=hkv, causal=causal,
-                              layout=AttentionInputLayout.head_major, qk_norm=qk_norm,
-                              q_norm_weight=q_norm_weight, k_norm_weight=k_norm_weight,
-                              rope_table=rope_table, eps=eps, kv_valid_len=kv_valid_len,
-                              kv_valid_lens=kv_valid_lens, scale=scale, batch=b)
-        for name, t in (("q", q), ("k", k), ("v", v), ("o", out)):
-            sb, st, sh, sd = t.stride()
-            if sd != 1:
-                raise AttentionValidationError(_lib.ERR_INVALID_ARG, "head_dim must be contiguous")
-            setattr(desc, f"{name}_batch_stride", sb)
-            setattr(desc, f"{name}_tok_stride", st)
-            setattr(desc, f"{name}_head_stride", sh)
+        key = (q.shape, k.shape, q.stride(), k.stride(), v.stride(), out.stride(), causal, qk_norm,
+               None if rope_table is None else (rope_table.data_ptr(), rope_table.numel()),
+               None if q_norm_weight is None else q_norm_weight.data_ptr(),
+               None if k_norm_weight is None else k_norm_weight.data_ptr(), eps, kv_valid_len,
+               None if kv_valid_lens is None else kv_valid_lens.data_ptr(), scale)
+        desc = self._desc_cache.get(key)
+        if desc is None:
+            b, sq, h, d = q.shape
+            sk, hkv = k.shape[1], k.shape[2]
+            desc = self.make_desc(heads=h, query_count=sq, key_count=sk, head_dim=d,
+                                  key_value_heads=hkv, causal=causal,
+                                  layout=AttentionInputLayout.head_major, qk_norm=qk_norm,
+                                  q_norm_weight=q_norm_weight, k_norm_weight=k_norm_weight,
+                                  rope_table=rope_table, eps=eps, kv_valid_len=kv_valid_len,
+                                  kv_valid_lens=kv_valid_lens, scale=scale, batch=b)
+            for name, t in (("q", q), ("k", k), ("v", v), ("o", out)):
+                sb, st, sh, sd = t.stride()
+                if sd != 1:
+                    raise AttentionValidationError(_lib.ERR_INVALID_ARG, "head_dim must be contiguous")
+                setattr(desc, f"{name}_batch_stride", sb)
+                setattr(desc, f"{name}_tok_stride", st)
+                setattr(desc, f"{name}_head_stride", sh)
+            if len(self._desc_cache) > 256:
+                self._desc_cache.clear()
+            self._desc_cache[key] = desc
         if stream is None:
             stream = torch.cuda.current_stream(q.device)
         rc = self._lib.animaxs_attn_forward(self._ctx, ctypes.byref(desc), q.data_ptr(), k.data_ptr(),
