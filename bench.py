@@ -353,8 +353,9 @@ def profile_kernel(args):
     shape = (4, S_SELF, HEADS, HD)
     q, k, v = (torch.randn(*shape, generator=g, device="cuda").half() for _ in range(3))
     out = torch.empty_like(q)
+    rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).cuda()
     for _ in range(args.warmup + args.steps):
-        ex.attention(q, k, v, out=out)
+        ex.attention(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope)
     torch.cuda.synchronize()
     ex.synchronize()
     print("profile-kernel done", flush=True)
@@ -369,8 +370,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernel", action="store_true",
-                    help="only launch the flash kernel on a batch-4 4096-token self-attention "
-                         "(192 MiB of inputs, > L2): the small case for ncu captures")
+                    help="only run the fused rms+rope3d self-attention (prologue + flash kernel) "
+                         "on a batch-4 4096-token case (192 MiB of inputs, > L2): the small "
+                         "case for ncu captures")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
