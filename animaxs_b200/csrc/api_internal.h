@@ -6,6 +6,7 @@
 
 #include <cstdint>
 #include <string>
+#include <vector>
 
 #include "../../include/animaxs_attn.h"
 
@@ -18,6 +19,9 @@ struct animaxs_attn_ctx {
   size_t staging_bytes = 0;
   unsigned int* d_status = nullptr;  // device status word written by kernels
   int64_t query_tiles = 0;
+  bool timing = false;                        // bracket each attention kernel with events
+  std::vector<cudaEvent_t> events;            // pool: pairs (start, stop)
+  size_t events_used = 0;                     // events recorded since the last read
   std::string last_error;
 };
 

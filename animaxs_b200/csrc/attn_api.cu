@@ -107,6 +107,7 @@ extern "C" int animaxs_attn_destroy(animaxs_attn_ctx* ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->staging) cudaFree(ctx->staging);
   if (ctx->d_status) cudaFree(ctx->d_status);
+  for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
   cudaSetDevice(prev);
   delete ctx;
   return ANIMAXS_OK;
@@ -404,8 +405,24 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     p.o_batch = d->o_batch_stride;
   }
   p.status = ctx->d_status;
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+  if (ctx->timing) {
+    while (ctx->events.size() < ctx->events_used + 2) {
+      cudaEvent_t ev;
+      cudaError_t ce = cudaEventCreate(&ev);
+      if (ce != cudaSuccess) return ax_cuda_fail(ctx, ce, "timing event");
+      ctx->events.push_back(ev);
+    }
+    ev_start = ctx->events[ctx->events_used];
+    ev_stop = ctx->events[ctx->events_used + 1];
+    cudaEventRecord(ev_start, stream);
+  }
   cudaError_t e = ax::launch_attn_fwd(tq, tk, tv, p, heads_count, d->batch, stream);
   if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "attention launch");
+  if (ctx->timing) {
+    cudaEventRecord(ev_stop, stream);
+    ctx->events_used += 2;
+  }
   ctx->query_tiles += static_cast<int64_t>(heads_count) * d->batch *
                       ((d->q_len + ax::kTileM - 1) / ax::kTileM);
   return ANIMAXS_OK;
@@ -436,6 +453,34 @@ extern "C" int animaxs_attn_synchronize(animaxs_attn_ctx* ctx, void* stream) {
   if (status & ax::kStatusTimeoutBit)
     return ax_set_error(ctx, ANIMAXS_ERR_TIMEOUT, "a bounded device-side wait expired");
   if (status != 0) return ax_set_error(ctx, ANIMAXS_ERR_CUDA, "device status 0x%x", status);
+  return ok(ctx);
+}
+
+extern "C" int animaxs_attn_set_kernel_timing(animaxs_attn_ctx* ctx, int enable) {
+  if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
+  ctx->timing = enable != 0;
+  return ANIMAXS_OK;
+}
+
+extern "C" int animaxs_attn_kernel_timing(animaxs_attn_ctx* ctx, int64_t* launches,
+                                          double* total_ms, double* max_ms) {
+  if (ctx == nullptr || launches == nullptr || total_ms == nullptr || max_ms == nullptr)
+    return ANIMAXS_ERR_INVALID_ARG;
+  *launches = 0;
+  *total_ms = 0.0;
+  *max_ms = 0.0;
+  if (ctx->events_used == 0) return ok(ctx);
+  cudaError_t e = cudaEventSynchronize(ctx->events[ctx->events_used - 1]);
+  if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "timing read");
+  for (size_t i = 0; i + 1 < ctx->events_used; i += 2) {
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, ctx->events[i], ctx->events[i + 1]);
+    if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "timing elapsed");
+    *launches += 1;
+    *total_ms += ms;
+    if (ms > *max_ms) *max_ms = ms;
+  }
+  ctx->events_used = 0;
   return ok(ctx);
 }
 

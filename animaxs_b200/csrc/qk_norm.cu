@@ -17,13 +17,11 @@
 namespace ax {
 namespace {
 
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 128;
 
-__device__ __forceinline__ void norm_row(const __half* src, __half* dst, const __half* weight,
-                                         float eps, bool rope, const float (&c)[8],
-                                         const float (&ns)[8], const float (&sn)[8], int l16,
-                                         unsigned mask) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ void norm_row(uint4 raw, __half* dst, const __half* weight, float eps,
+                                         bool rope, const float (&c)[8], const float (&ns)[8],
+                                         const float (&sn)[8], int l16, unsigned mask) {
   const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
   float x[8];
 #pragma unroll
@@ -72,6 +70,10 @@ __device__ __forceinline__ void norm_row(const __half* src, __half* dst, const _
   *reinterpret_cast<uint4*>(dst) = res;
 }
 
+// One CTA per (token, batch).  The token's rows -- every q head, then every k
+// head -- are dealt to the 8 half-warps four at a time; a half-warp issues its
+// four 128-bit loads before doing any math so that enough bytes are in flight
+// to cover HBM latency.
 __global__ void __launch_bounds__(kNormThreads) qk_norm_kernel(const NormParams p) {
   const int tok = blockIdx.x;
   const int bb = blockIdx.y;
@@ -94,16 +96,37 @@ __global__ void __launch_bounds__(kNormThreads) qk_norm_kernel(const NormParams 
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i] = ns[i] = sn[i] = 0.f;
   }
+  const NormJob& J0 = p.job[0];
+  const NormJob& J1 = p.job[1];
+  const int r0 = (tok < J0.tokens && bb < J0.batch) ? J0.heads : 0;
+  const int r1 = (p.njobs > 1 && tok < J1.tokens && bb < J1.batch) ? J1.heads : 0;
+  const int rows = r0 + r1;
+  constexpr int kHalfWarps = kNormThreads / 16;
+  constexpr int kUnroll = 4;
+  for (int base = 0; base < rows; base += kHalfWarps * kUnroll) {
+    uint4 raw[kUnroll];
+    __half* dst[kUnroll];
+    const __half* w[kUnroll];
 #pragma unroll
-  for (int jb = 0; jb < 2; ++jb) {
-    if (jb >= p.njobs) break;
-    const NormJob& J = p.job[jb];
-    if (tok >= J.tokens || bb >= J.batch) continue;
-    const __half* in = J.in + bb * J.in_batch + static_cast<long long>(tok) * J.in_tok + l16 * 8;
-    __half* out = J.out + bb * J.out_batch + static_cast<long long>(tok) * J.out_tok + l16 * 8;
-    for (int hh = hw; hh < J.heads; hh += kNormThreads / 16)
-      norm_row(in + hh * J.in_head, out + hh * J.out_head, J.weight, p.eps, rope, c, ns, sn, l16,
-               mask);
+    for (int u = 0; u < kUnroll; ++u) {
+      const int r = base + hw + kHalfWarps * u;
+      dst[u] = nullptr;
+      w[u] = nullptr;
+      if (r < rows) {
+        const bool second = r >= r0;
+        const NormJob& J = second ? J1 : J0;
+        const int head = second ? r - r0 : r;
+        const __half* src = J.in + bb * J.in_batch + static_cast<long long>(tok) * J.in_tok +
+                            static_cast<long long>(head) * J.in_head + l16 * 8;
+        dst[u] = J.out + bb * J.out_batch + static_cast<long long>(tok) * J.out_tok +
+                 static_cast<long long>(head) * J.out_head + l16 * 8;
+        w[u] = J.weight;
+        raw[u] = *reinterpret_cast<const uint4*>(src);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      if (dst[u] != nullptr) norm_row(raw[u], dst[u], w[u], p.eps, rope, c, ns, sn, l16, mask);
   }
 }
 

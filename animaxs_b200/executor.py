@@ -149,6 +149,17 @@ class AttentionExecutor:
         self._check(self._lib.animaxs_attn_query_tiles(self._ctx, ctypes.byref(v)))
         return v.value
 
+    def set_kernel_timing(self, enable: bool):
+        """Bracket every flash-kernel launch with CUDA events (see kernel_timing)."""
+        self._check(self._lib.animaxs_attn_set_kernel_timing(self._ctx, 1 if enable else 0))
+
+    def kernel_timing(self):
+        """(launches, total_ms, max_ms) of the flash kernel since the last read."""
+        n, tot, mx = ctypes.c_int64(), ctypes.c_double(), ctypes.c_double()
+        self._check(self._lib.animaxs_attn_kernel_timing(self._ctx, ctypes.byref(n), ctypes.byref(tot),
+                                                         ctypes.byref(mx)))
+        return n.value, tot.value, mx.value
+
     def make_desc(self, *, heads, query_count, key_count, head_dim, key_value_heads=None,
                   causal=False, layout=None, qk_norm="none", q_norm_weight=None,
                   k_norm_weight=None, rope_table=None, eps=1e-6, kv_valid_len=None,

@@ -157,6 +157,18 @@ int animaxs_attn_scratch_bytes(const animaxs_attn_desc* desc, int64_t* bytes);
  * MetricsCollector.recordAttentionQueryTile (GenerationMetrics.swift:490-510). */
 int animaxs_attn_query_tiles(const animaxs_attn_ctx* ctx, int64_t* tiles);
 
+/* Opt-in GPU timing of the flash-attention kernel: when enabled, every
+ * animaxs_attn_forward on this context brackets the attention kernel (not the
+ * q/k prologue) with a pair of CUDA events on the caller's stream.
+ * animaxs_attn_kernel_timing waits for the recorded events, returns the
+ * launch count, the summed and the largest per-launch time in milliseconds,
+ * and clears the record.  Counterpart of the reference's GPU stage timers
+ * (MetricsCollector, GenerationMetrics.swift:325-610, fed from
+ * command.gpuStartTime/gpuEndTime, DiTBlockExecutor.swift:265-270). */
+int animaxs_attn_set_kernel_timing(animaxs_attn_ctx* ctx, int enable);
+int animaxs_attn_kernel_timing(animaxs_attn_ctx* ctx, int64_t* launches, double* total_ms,
+                               double* max_ms);
+
 /* Standalone per-(token, head) RMSNorm + split-half RoPE, fp16 in/out
  * ([tokens, heads, head_dim] rows, `row_stride` elements apart per token),
  * in place allowed.  Replaces kernel rms_rope_split_half
