@@ -27,6 +27,8 @@
 // softmax warpgroup works on its tile, the tensor core runs the other tile's
 // MMAs.  tcgen05.mma ops from one thread execute in issue order, which is what
 // lets QK_X(j+1) overwrite the TMEM columns PV_X(j) reads P_X(j) from.
+#include <atomic>
+
 #include "kernels.h"
 #include "sm100_ptx.cuh"
 
@@ -368,12 +370,17 @@ int attn_fwd_rows_per_cta() { return 2 * kTileM; }
 cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const AttnFwdParams& p, int heads_in_launch, int batch,
                             cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_sm100_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  // The dynamic shared-memory opt-in is a per-device function attribute.
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((configured.load(std::memory_order_acquire) & bit) == 0) {
+    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   dim3 grid(p.n_q_tiles, heads_in_launch, batch);
   attn_fwd_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);

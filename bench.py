@@ -1,10 +1,12 @@
 """Benchmark: the AnimaXS DiT attention workload (configuration 4) on B200.
 
-One "step" = one image per GPU through the full 8-step DiT attention workload
-at 1024x1024: 8 Euler steps x 28 blocks x (4096-token self-attention with q/k
-RMSNorm + 3-D RoPE (1x64x64), then 4096x512 cross-attention with q/k RMSNorm),
-16 heads x 128.  Images are independent, so N GPUs each process their own
-image per step (weak scaling, no data-path collective).
+One "step" = one batch of 8 images per GPU (configuration 4's batch of 8
+prompts) through the full 8-step DiT attention workload at 1024x1024: 8 Euler
+steps x 28 blocks x (4096-token self-attention with q/k RMSNorm + 3-D RoPE
+(1x64x64), then 4096x512 cross-attention with q/k RMSNorm), 16 heads x 128;
+every attention call carries the whole batch.  Images are independent, so N
+GPUs each process their own batch of 8 (weak scaling, no data-path
+collective); N=1 is configuration 4 exactly.
 
 Printed JSON line (rank 0):
   value       images/s for the whole job, inputs resident in HBM
@@ -42,7 +44,8 @@ CALLS_PER_IMAGE = BLOCKS * EULER_STEPS            # 224 (self, cross) pairs
 SELF_FLOPS = 4.0 * S_SELF * S_SELF * HD * HEADS   # 137.4 GFLOP per self-attention
 CROSS_FLOPS = 4.0 * S_SELF * S_CTX * HD * HEADS   # 17.2 GFLOP per cross-attention
 IMAGE_FLOPS = CALLS_PER_IMAGE * (SELF_FLOPS + CROSS_FLOPS)
-POOL_BLOCKS = 6                                   # distinct resident input sets (> L2)
+BATCH = 8                                         # images per GPU per step (config 4)
+POOL_BLOCKS = 3                                   # distinct resident input sets (> L2)
 
 METRIC = ("DiT attention throughput, 8-step 1024x1024 workload "
           "(28 blocks x 8 steps x [4096-tok self rms+rope3d + 4096x512 cross rms])")
@@ -154,8 +157,9 @@ def make_pool(torch, device, seed):
         def r(*shape):
             return torch.randn(*shape, generator=g, device=device, dtype=torch.float32).half()
         pool.append({
-            "sq": r(1, S_SELF, HEADS, HD), "sk": r(1, S_SELF, HEADS, HD), "sv": r(1, S_SELF, HEADS, HD),
-            "cq": r(1, S_SELF, HEADS, HD), "ck": r(1, S_CTX, HEADS, HD), "cv": r(1, S_CTX, HEADS, HD),
+            "sq": r(BATCH, S_SELF, HEADS, HD), "sk": r(BATCH, S_SELF, HEADS, HD),
+            "sv": r(BATCH, S_SELF, HEADS, HD), "cq": r(BATCH, S_SELF, HEADS, HD),
+            "ck": r(BATCH, S_CTX, HEADS, HD), "cv": r(BATCH, S_CTX, HEADS, HD),
         })
     return pool
 
@@ -175,7 +179,7 @@ def run_gpu(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(device)
     rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).to(device)
     pool = make_pool(torch, device, 1234 + rank)
-    o_self = torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16, device=device)
+    o_self = torch.empty(BATCH, S_SELF, HEADS, HD, dtype=torch.float16, device=device)
     o_cross = torch.empty_like(o_self)
 
     def image():
@@ -221,7 +225,7 @@ def run_gpu(args, rank, world, local_rank):
         t = torch.tensor([elapsed_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
-    images = args.steps * world
+    images = args.steps * world * BATCH
     value = images / (elapsed_ms / 1e3)
     launches = args.steps * CALLS_PER_IMAGE * 4   # per block: 2 x (q/k prologue + flash kernel)
 
@@ -232,22 +236,23 @@ def run_gpu(args, rank, world, local_rank):
         return
     peak_burst, peak_sust, hbm, peak_kind = peaks()
     avg_kern = kern_total_ms / n_kern if n_kern else float("nan")
-    achieved = SELF_FLOPS / (avg_kern / 1e3) / 1e12
+    achieved = BATCH * SELF_FLOPS / (avg_kern / 1e3) / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-        "config": {"workload": "config4: 8-step DiT attention @1024^2 (224 self 4096 + 224 cross 4096x512 per image)",
-                   "images_per_gpu_per_step": 1, "global_batch": world, "seq_len": S_SELF,
+        "config": {"workload": "config4: 8-step DiT attention @1024^2, batch of 8 prompts per GPU "
+                               "(224 self 4096 + 224 cross 4096x512 calls per step, each over the batch)",
+                   "images_per_gpu_per_step": BATCH, "global_batch": BATCH * world, "seq_len": S_SELF,
                    "ctx_len": S_CTX, "heads": HEADS, "head_dim": HD, "parallelism": f"batch-shard x{world}",
-                   "l2": f"inputs cycled over a {POOL_BLOCKS * 68} MiB resident pool (> 126 MB L2)"},
-        "tflops_per_gpu": IMAGE_FLOPS * args.steps / (elapsed_ms / 1e3) / 1e12,
-        "frac_of_peak_per_gpu": IMAGE_FLOPS * args.steps / (elapsed_ms / 1e3) / 1e12 / peak_sust,
-        "roofline": {"kernel": "attn_fwd_sm100_kernel (4096-token self-attention, 16 heads)",
+                   "l2": f"inputs cycled over a {POOL_BLOCKS * 68 * BATCH} MiB resident pool (> 126 MB L2)"},
+        "tflops_per_gpu": BATCH * IMAGE_FLOPS * args.steps / (elapsed_ms / 1e3) / 1e12,
+        "frac_of_peak_per_gpu": BATCH * IMAGE_FLOPS * args.steps / (elapsed_ms / 1e3) / 1e12 / peak_sust,
+        "roofline": {"kernel": "attn_fwd_sm100_kernel (4096-token self-attention, batch 8, 16 heads)",
                      "bound": "tensor", "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
                      "frac": achieved / peak_sust, "peak_kind": f"{peak_kind} bf16 dense, sustained",
                      "frac_of_burst_peak": achieved / peak_burst,
-                     "flops_per_launch": SELF_FLOPS, "avg_launch_ms": avg_kern,
+                     "flops_per_launch": BATCH * SELF_FLOPS, "avg_launch_ms": avg_kern,
                      "max_launch_ms": kern_max_ms, "launches_timed": n_kern,
                      "traffic": None},
         "clocks": clocks,
@@ -329,7 +334,7 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
         t = torch.tensor([el], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         el = float(t.item())
-    return {"value": steps * world / el, "unit": "img/s",
+    return {"value": steps * world / el, "unit": "img/s", "images_per_call": 1,
             "h2d_bytes_per_step": h2d * CALLS_PER_IMAGE, "d2h_bytes_per_step": d2h * CALLS_PER_IMAGE,
             "steps": steps, "path": "AttentionExecutor.attention -> animaxs_attn_forward (fused rms/rope)"}
 
