@@ -1,0 +1,152 @@
+"""CPU tests of the C ABI: the library loads, exports every function the header
+declares, and its host-side logic (validation mirroring
+AttentionExecutor.validate, RoPE tables, GQA map, scratch sizing) works
+without a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import attn_oracle as ora
+from tests.conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "animaxs_attn.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(animaxs_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from animaxs_b200 import _lib
+    return _lib.lib()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from animaxs_b200 import _lib
+    names = _declared()
+    assert len(names) >= 20
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (animaxs_\w+)", out))
+    missing = [n for n in names if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    # and the ctypes binding knows every one of them
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+    assert lib.animaxs_attn_abi_version() == 1
+
+
+def test_library_links_no_nccl_or_cudart_at_load_time():
+    from animaxs_b200 import _lib
+    out = subprocess.run(["ldd", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libnccl" not in out and "libcudart" not in out
+
+
+def test_create_fails_cleanly_without_gpu(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    ctx = ctypes.c_void_p()
+    assert lib.animaxs_attn_create(0, ctypes.byref(ctx)) == -6  # ANIMAXS_ERR_NO_DEVICE
+    assert not ctx.value
+
+
+def _desc(lib, **kw):
+    from animaxs_b200._lib import AttnDesc
+    d = AttnDesc()
+    lib.animaxs_attn_desc_init(ctypes.byref(d), kw.pop("batch", 1), kw.pop("heads", 16),
+                               kw.pop("kv_heads", 16), kw.pop("q_len", 1024),
+                               kw.pop("kv_len", 1024), kw.pop("head_dim", 128))
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def _validate(lib, d, ptrs=(0x1000, 0x2000, 0x3000, 0x4000)):
+    return lib.animaxs_attn_validate(None, ctypes.byref(d), *[ctypes.c_void_p(p) for p in ptrs])
+
+
+def test_validation_mirrors_reference(lib):
+    ok = _desc(lib)
+    assert _validate(lib, ok) == 0
+    # shape rules (AttentionExecutor.swift:784-789)
+    assert _validate(lib, _desc(lib, heads=6, kv_heads=4)) == -1
+    assert _validate(lib, _desc(lib, q_len=0)) == -1
+    assert _validate(lib, _desc(lib, causal=1, q_len=100, kv_len=200)) == -1
+    assert _validate(lib, _desc(lib, causal=1, q_len=100, kv_len=100)) == 0
+    # unsupported head dim
+    assert _validate(lib, _desc(lib, head_dim=64)) == -2
+    # null and misaligned buffers, misaligned stride
+    assert _validate(lib, ok, (0, 0x2000, 0x3000, 0x4000)) == -1
+    assert _validate(lib, ok, (0x1008, 0x2000, 0x3000, 0x4000)) == -1
+    assert _validate(lib, _desc(lib, q_tok_stride=2047 * 1)) == -1
+    # buffer range (:808-823): q needs 1024*2048*2 bytes
+    assert _validate(lib, _desc(lib, q_bytes=1024 * 2048 * 2)) == 0
+    assert _validate(lib, _desc(lib, q_bytes=1024 * 2048 * 2 - 2)) == -3
+    # masks, scale, rope
+    assert _validate(lib, _desc(lib, kv_valid_len=1025)) == -1
+    assert _validate(lib, _desc(lib, kv_valid_len=-1)) == -1
+    assert _validate(lib, _desc(lib, scale=-1.0)) == -1
+    assert _validate(lib, _desc(lib, qk_norm=2)) == -1            # rope table missing
+    assert _validate(lib, _desc(lib, qk_norm=2, rope_table=0x5000, rope_rows=1023)) == -1
+    assert _validate(lib, _desc(lib, qk_norm=2, rope_table=0x5000, rope_rows=1024)) == 0
+    assert _validate(lib, _desc(lib, qk_norm=7)) == -1
+    # overflow
+    assert _validate(lib, _desc(lib, q_batch_stride=1 << 45, batch=2)) == -8
+
+
+def test_scratch_bytes(lib):
+    d = _desc(lib, qk_norm=1, q_len=4096, kv_len=512)
+    n = ctypes.c_int64()
+    assert lib.animaxs_attn_scratch_bytes(ctypes.byref(d), ctypes.byref(n)) == 0
+    assert n.value == 4096 * 16 * 256 + 512 * 16 * 256
+    d.qk_norm = 0
+    lib.animaxs_attn_scratch_bytes(ctypes.byref(d), ctypes.byref(n))
+    assert n.value == 0
+
+
+@pytest.mark.parametrize("grid", [(1, 32, 32), (1, 64, 64), (2, 8, 12)])
+def test_rope3d_table_helper(grid):
+    from animaxs_b200 import DitRoPE
+    got = DitRoPE.generate(*grid).reshape(-1, 64, 2, 2)
+    np.testing.assert_allclose(got, ora.dit_rope_table(*grid), atol=3e-6)
+
+
+def test_rope1d_table_helper():
+    from animaxs_b200 import qwen_rope
+    got = qwen_rope(512).reshape(512, 64, 2, 2)
+    np.testing.assert_allclose(got, ora.rope1d_table(512, 1e6), atol=4e-5)
+
+
+def test_gqa_helper():
+    from animaxs_b200 import AttentionValidationError, GqaHeadMapping
+    assert [GqaHeadMapping.kv_head(h, 16, 8) for h in range(16)] == [ora.gqa_kv_head(h, 16, 8) for h in range(16)]
+    with pytest.raises(AttentionValidationError):
+        GqaHeadMapping.kv_head(0, 6, 4)
+
+
+def test_executor_mirror_errors_without_gpu():
+    """The Python mirror raises the reference's validation messages before any GPU work."""
+    from animaxs_b200 import AttentionExecutor, AttentionInputLayout, AttentionValidationError
+    ex = AttentionExecutor.__new__(AttentionExecutor)
+    from animaxs_b200 import _lib
+    ex._lib = _lib.lib()
+    ex.layout = AttentionInputLayout.head_major
+    ex.numerics = "legacy"
+    ex.tile_rows = 128
+    with pytest.raises(AttentionValidationError, match="keyValueHeads == heads"):
+        ex.make_desc(heads=2, query_count=4, key_count=4, head_dim=64, key_value_heads=1,
+                     layout=AttentionInputLayout.token_major(128))
+    assert ex.maximum_score_scratch_bytes(1024) == 128 * 1024 * 2
+    assert ex.maximum_score_scratch_bytes(37, 19) == 19 * 37 * 2
+    ex.numerics = "fp32ScoresAndSoftmax"
+    assert ex.maximum_score_scratch_bytes(37, 19) == 19 * 37 * 4
+    with pytest.raises(AttentionValidationError, match="token-major"):
+        ex.make_desc(heads=2, query_count=4, key_count=4, head_dim=64,
+                     layout=AttentionInputLayout.token_major(128))
