@@ -20,6 +20,7 @@ ERR_TIMEOUT = -5
 ERR_NO_DEVICE = -6
 ERR_NCCL = -7
 ERR_OVERFLOW = -8
+ERR_SCRATCH_LIMIT = -9
 
 QK_NONE, QK_RMS, QK_RMS_ROPE = 0, 1, 2
 
@@ -47,7 +48,7 @@ class AttentionDeviceError(AttentionError):
 def raise_for(status: int, message: str):
     if status == OK:
         return
-    if status in (ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_OOB, ERR_OVERFLOW):
+    if status in (ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_OOB, ERR_OVERFLOW, ERR_SCRATCH_LIMIT):
         raise AttentionValidationError(status, message)
     if status == ERR_TIMEOUT:
         raise AttentionTimeoutError(status, message)
@@ -100,6 +101,7 @@ SIGNATURES = {
     "animaxs_comm_create": (_I, [_P, _I, _I, _P, ctypes.POINTER(_P)]),
     "animaxs_comm_destroy": (_I, [_P]),
     "animaxs_attn_forward_head_sharded": (_I, [_P, _P, _DESC, _P, _P, _P, _P, _P]),
+    "animaxs_attn_forward_noalloc": (_I, [_DESC, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

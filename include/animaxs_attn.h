@@ -52,7 +52,8 @@ typedef enum animaxs_status {
   ANIMAXS_ERR_TIMEOUT = -5,     /* a bounded device-side wait expired */
   ANIMAXS_ERR_NO_DEVICE = -6,   /* no sm_100 device */
   ANIMAXS_ERR_NCCL = -7,        /* NCCL unavailable or a collective failed */
-  ANIMAXS_ERR_OVERFLOW = -8     /* "attention byte size overflow" (:830-838) */
+  ANIMAXS_ERR_OVERFLOW = -8,    /* "attention byte size overflow" (:830-838) */
+  ANIMAXS_ERR_SCRATCH_LIMIT = -9 /* call needs more than animaxs_attn_forward_noalloc's fixed scratch */
 } animaxs_status;
 
 /* q/k normalisation fused in front of the attention.
@@ -200,6 +201,28 @@ int animaxs_rope1d_table(int seq_len, int head_dim, double theta, float* out);
  * (AttentionExecutor.swift:222; GqaHeadMappingTests.swift:17-21).
  * Returns < 0 (ANIMAXS_ERR_INVALID_ARG) if heads is not a multiple of kv_heads. */
 int animaxs_gqa_kv_head(int query_head, int heads, int kv_heads);
+
+/* Allocation-free variant of animaxs_attn_forward.  No counterpart exists in
+ * the reference; it is for callers that must not have device memory allocated
+ * behind their back -- an application that reserves the device's memory up
+ * front, a host runtime whose allocator owns every device allocation, or a
+ * latency-critical loop in which an allocation (which may synchronise the
+ * device) is unacceptable.  It runs the same kernels, but the normalised q/k
+ * copies of the fused prologue live in one fixed 32 MiB device array that
+ * every GPU loading the library holds until the process exits; it takes no
+ * context and allocates nothing.  Works on the CURRENT device.
+ *  - A call needing more than 32 MiB of normalised q/k (see
+ *    animaxs_attn_scratch_bytes) fails with ANIMAXS_ERR_SCRATCH_LIMIT, e.g. the
+ *    16384-token self-attention; qk_norm = NONE needs none.
+ *  - All calls on a device share the array and it keeps the last call's
+ *    contents (every byte read is rewritten first); calls that overlap on the
+ *    GPU race on it, so serialise them.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress); make that call before any stream capture.
+ *  - Returns status codes only (no last-error text); device-side wait
+ *    timeouts are not reported. */
+int animaxs_attn_forward_noalloc(const animaxs_attn_desc* desc, const void* q, const void* k,
+                                 const void* v, void* o, void* stream);
 
 /* ---- Multi-GPU: heads sharded across ranks + one NCCL all-gather ----------
  * No counterpart exists in the reference (a single-device app); this serves
