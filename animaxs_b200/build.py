@@ -44,6 +44,26 @@ def _headers():
     return hs
 
 
+def check_register_split(source: str, ptxas_log: str) -> None:
+    """The flash kernel re-splits its registers with setmaxnreg; the raise waits
+    until enough registers are free in the CTA's launch allocation, so the new
+    shares must fit into (threads x registers ptxas gave each thread at launch).
+    Refuse to build otherwise."""
+    import re
+    text = open(source).read()
+    soft = int(re.search(r"#define AX_SOFTMAX_REGS (\d+)", text).group(1))
+    other = int(re.search(r"#define AX_OTHER_REGS (\d+)", text).group(1))
+    threads = int(re.search(r"constexpr int kThreads = (\d+);", text).group(1))
+    m = re.search(r"attn_fwd_sm100_kernel.*?Used (\d+) registers", ptxas_log, re.S)
+    if m is None:
+        raise RuntimeError("could not read the flash kernel's register count from ptxas")
+    launch = int(m.group(1))
+    need = 2 * 128 * soft + (threads - 256) * other
+    if need > threads * launch or soft % 8 or other % 8:
+        raise RuntimeError(f"register split {2}x128x{soft} + {threads - 256}x{other} = {need} "
+                           f"exceeds the launch allocation {threads}x{launch} = {threads * launch}")
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     cc = nvcc()
@@ -65,6 +85,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         for cmd, res in logs:
             sys.stderr.write(f"--- {os.path.basename(cmd[-3])}\n{res.stderr}")
+    for cmd, res in logs:
+        if cmd[-3].endswith("attn_fwd_sm100.cu"):
+            check_register_split(cmd[-3], res.stderr)
     if force or jobs or not _newer(LIB, objs):
         link = [cc, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-ldl", "-Xcompiler", "-fPIC"]
         res = subprocess.run(link, capture_output=True, text=True)

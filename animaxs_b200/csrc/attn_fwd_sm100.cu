@@ -8,25 +8,21 @@
 // computed as an online (flash) softmax over 128-key tiles.
 //
 // One CTA = two 128-row query tiles (A: rows q0..q0+127, B: q0+128..q0+255) of
-// one (batch, head); both stream the same K/V tiles.  Eighteen warps:
-//   warps 0-7  softmax for tile A, warps 8-15 softmax for tile B.  Each query
-//              row (= TMEM lane) is shared by two threads, one per 64-column
-//              half of S: warps 0-3 / 8-11 own columns [0,64), warps 4-7 /
-//              12-15 columns [64,128).  Per K/V tile a thread reads its half
-//              row of S from TMEM, applies the causal / key-padding masks,
-//              exchanges its partial row max with its partner through shared
-//              memory (an mbarrier handshake), updates the running max
-//              (lazily: O is only rescaled when the max grows by more than
-//              2^8) and its partial sum in fp32, and writes P = exp2(S*c - m)
-//              as fp16 into TMEM over its own consumed S columns.  At the end
-//              the partners add their sums and each normalises and stores its
-//              half of the O row.
-//   warp 16    MMA issuer + TMEM owner: S_X = Q_X K_j^T (tcgen05.mma kind::f16,
+// one (batch, head); both stream the same K/V tiles.  Twelve warps:
+//   warps 0-3  softmax for tile A, warps 4-7 softmax for tile B: thread t owns
+//              query row t of its tile (= TMEM lane t).  Per K/V tile it reads
+//              S from TMEM, applies the causal / key-padding masks, updates the
+//              running max (lazily: O is only rescaled when the max grows by
+//              more than 2^8) and sum in fp32, and writes P = exp2(S*c - m) as
+//              fp16 back into TMEM over the consumed S columns.  At the end it
+//              normalises O and stores it.
+//   warp 8     MMA issuer + TMEM owner: S_X = Q_X K_j^T (tcgen05.mma kind::f16,
 //              both operands in shared memory) and O_X += P_X V_j with P read
 //              straight from TMEM (A operand in TMEM).
-//   warp 17    TMA producer: both Q tiles once, then K_j / V_j into 2-stage rings.
-// TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512);
-// P_X (fp16 pairs) overlays S_X columns [0,32) (keys 0-63) and [64,96) (keys 64-127).
+//   warp 9     TMA producer: both Q tiles once, then K_j / V_j into 2-stage rings.
+//   warps 10-11 idle (they complete the third warpgroup for setmaxnreg).
+// TMEM (512 columns): S_A [0,128), S_B [128,256) (P_X overlays the first 64
+// columns of S_X), O_A [256,384), O_B [384,512).
 //
 // The tensor core alternates PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): while one
 // softmax warpgroup works on its tile, the tensor core runs the other tile's
@@ -46,11 +42,8 @@ constexpr uint32_t kSmQ = 0;                            // Q_A, Q_B
 constexpr uint32_t kSmK = kSmQ + 2 * kTileBytes;        // 2 stages
 constexpr uint32_t kSmV = kSmK + 2 * kTileBytes;        // 2 stages
 constexpr uint32_t kSmBar = kSmV + 2 * kTileBytes;
-constexpr uint32_t kSmXchg = kSmBar + 256;             // [parity][tile][half][128] floats
-constexpr uint32_t kSmemBytes = kSmXchg + 2 * 2 * 2 * 128 * 4 + 1024;  // + alignment slack
-constexpr int kThreads = 18 * 32;
-constexpr int kWarpMma = 16;
-constexpr int kWarpTma = 17;
+constexpr uint32_t kSmemBytes = kSmBar + 256 + 1024;    // + barriers + alignment slack
+constexpr int kThreads = 384;  // warpgroups: softmax A, softmax B, MMA/TMA (+2 idle warps)
 
 enum : int {
   kBarQ = 0,
@@ -59,11 +52,10 @@ enum : int {
   kBarVFull = 5,   // +stage
   kBarVEmpty = 7,  // +stage
   kBarSFull = 9,   // +tile
-  kBarPFull = 11,  // +tile (256 arrivals)
+  kBarPFull = 11,  // +tile (128 arrivals)
   kBarODone = 13,  // +tile
   kBarDone = 15,
-  kBarXchg = 16,   // +tile*4 + row quarter (64 arrivals: the two half-row warps)
-  kNumBars = 24
+  kNumBars = 16
 };
 constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
@@ -74,12 +66,19 @@ constexpr uint32_t kIdescQK = idesc_f16_f32(128, 128, false);  // B = K tile, K-
 constexpr uint32_t kIdescPV = idesc_f16_f32(128, 128, true);   // B = V tile, MN-major
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled when max grows > 2^8
 // Of every 8 adjacent column pairs, this many take exp2 on the FMA pipe
-// (polynomial) and the rest on the MUFU pipe, so that neither limits the
-// softmax warps.
+// (polynomial) and the rest on the MUFU pipe.
 #ifndef AX_POLY_PAIRS
-#define AX_POLY_PAIRS 3
+#define AX_POLY_PAIRS 2
 #endif
 constexpr int kPolyPairsPer8 = AX_POLY_PAIRS;
+// Register split (setmaxnreg): the kernel launches 3 warpgroups at the
+// compiler's per-thread count N (ptxas: 168); the two softmax warpgroups raise
+// theirs to AX_SOFTMAX_REGS and the MMA/TMA warpgroup lowers its to
+// AX_OTHER_REGS.  2*128*AX_SOFTMAX_REGS + 128*AX_OTHER_REGS must not exceed
+// 384*N, or the raise would wait forever: build.py checks this against the
+// ptxas report before it links the library.
+#define AX_SOFTMAX_REGS 208
+#define AX_OTHER_REGS 88
 
 // 2^x on the FMA pipe for a pair of values.  Range reduction x = j + f with
 // j = round(x) obtained by adding 1.5*2^23 (the integer lands in the low
@@ -115,18 +114,24 @@ __device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile, int kk) {
   return sw128_desc(tile + kk * 2048, kPanelBytes, 1024);
 }
 
+// Descriptors advance by constant offsets of their start-address field
+// (bits 0-13, address >> 4; every operand lies below 256 KiB of shared memory,
+// so the field never carries).  The loops are unrolled: the MMA thread's issue
+// latency sits on the critical path whenever the tensor core waits for PV.
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint32_t k_tile) {
+  const uint64_t a0 = kmajor_desc(q_tile, 0), b0 = kmajor_desc(k_tile, 0);
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
-    umma_f16_ss(d_tmem, kmajor_desc(q_tile, kk), kmajor_desc(k_tile, kk), kIdescQK,
-                kk > 0 ? 1u : 0u);
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4);
+    umma_f16_ss(d_tmem, a0 + off, b0 + off, kIdescQK, kk > 0 ? 1u : 0u);
+  }
 }
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
                                          bool accumulate) {
+  const uint64_t b0 = vmajor_desc(v_tile, 0);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_f16_ts(d_tmem, p_tmem + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), vmajor_desc(v_tile, kk),
-                kIdescPV,
+    umma_f16_ts(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
                 (accumulate || kk > 0) ? 1u : 0u);
 }
 
@@ -168,20 +173,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv = max(nA, nB);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) {
-      uint32_t cnt = 1;
-      if (i == kBarPFull || i == kBarPFull + 1) cnt = 256;
-      if (i >= kBarXchg) cnt = 64;
-      mbar_init(BAR(i), cnt);
-    }
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(BAR(i), (i == kBarPFull || i == kBarPFull + 1) ? 128u : 1u);
     *abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == kWarpMma) {
+  if (warp == 8) {
     tmem_alloc(bar0 + kSlotTmem, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == kWarpTma && lane == 0) {
+  if (warp == 9 && lane == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -191,7 +192,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWarpTma) {
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(AX_OTHER_REGS));
+  if (warp == 9) {
     // ------------------------------------------------------------ producer --
     if (lane == 0 && n_kv > 0) {
       int armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (armed_v[st]) mbar_wait(BAR(kBarVFull + st), (armed_v[st] - 1) & 1, &local_abort, nullptr);
       }
     }
-  } else if (warp == kWarpMma) {
+  } else if (warp == 8) {
     // ----------------------------------------------------------------- MMA --
     if (lane == 0 && n_kv > 0) {
       const uint32_t sQA = sQ, sQB = sQ + kTileBytes;
@@ -286,20 +289,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int local_abort = 0;
       mbar_wait(BAR(kBarDone), 0, &local_abort, nullptr);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(AX_SOFTMAX_REGS));
     // ------------------------------------------------------------- softmax --
-    const int X = warp >> 3;                   // 0: tile A, 1: tile B
-    const int half = (warp >> 2) & 1;          // S / O columns [64*half, 64*half + 64)
-    const int t = ((warp & 3) << 5) | lane;    // row within the tile == TMEM lane
+    const int X = warp >> 2;              // 0: tile A, 1: tile B
+    const int t = threadIdx.x & 127;      // row within the tile == TMEM lane
     const int row = q0 + X * kTileM + t;
     const int nX = X ? nB : nA;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + X * 128 + half * 64;
-    const uint32_t o_addr = tmem + lane_base + kColO + X * 128 + half * 64;
-    const uint32_t xbar = BAR(kBarXchg + X * 4 + (warp & 3));
-    volatile float* xchg = reinterpret_cast<volatile float*>(gbase + kSmXchg);
-    // slot(parity, h): the value the half-h thread of this row published
-    auto slot = [&](int parity, int h) { return xchg + ((parity * 2 + X) * 2 + h) * 128 + t; };
+    const uint32_t s_addr = tmem + lane_base + X * 128;
+    const uint32_t o_addr = tmem + lane_base + kColO + X * 128;
     const float sl2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -308,33 +308,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[2][32];
+      uint32_t s[4][32];
       tmem_ld32(s_addr + 0, s[0]);
       tmem_ld32(s_addr + 32, s[1]);
+      tmem_ld32(s_addr + 64, s[2]);
+      tmem_ld32(s_addr + 96, s[3]);
       tmem_ld_wait(s[0]);
       asm volatile("" : AX_RW32(s[1])::"memory");
+      asm volatile("" : AX_RW32(s[2])::"memory");
+      asm volatile("" : AX_RW32(s[3])::"memory");
 
-      const int key0 = j * kTileN + half * 64;
-      if ((key0 + 64 > valid) || (p.causal && key0 + 63 > row)) {
+      const int key0 = j * kTileN;
+      if ((key0 + kTileN > valid) || (p.causal && key0 + kTileN - 1 > row)) {
         const int lim = p.causal ? min(valid, row + 1) : valid;  // keys >= lim are masked
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
+        for (int c = 0; c < 128; ++c)
           if (key0 + c >= lim) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      // Partial row max (8 independent chains), then combine with the partner.
+      // Row max with 8 independent chains.
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[0][i]);
 #pragma unroll
-      for (int c = 8; c < 64; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(s[c >> 5][c & 31]));
-      const float pmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      *slot(j & 1, half) = pmax;
-      mbar_arrive(xbar);
-      ok = mbar_wait(xbar, static_cast<uint32_t>(j & 1), abort_flag, p.status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      const float tmax = fmaxf(pmax, *slot(j & 1, half ^ 1)) * sl2;
+      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(s[c >> 5][c & 31]));
+      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
       const float m_new = fmaxf(m, tmax);
       const bool grow = m_new > m + kRescaleThreshold;  // also true on the first tile
       const float alpha = grow ? ex2_approx(m - m_new) : 1.f;  // 0 on the first tile (m = -inf)
@@ -347,34 +345,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float2 nmv = make_float2(neg_m, neg_m);
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                        make_float2(0.f, 0.f)};
-      uint32_t pk[32];
+      uint32_t pk[2][32];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float2 x = fma2(make_float2(__uint_as_float(s[c >> 5][c & 31]),
-                                          __uint_as_float(s[c >> 5][(c + 1) & 31])),
-                              sl2v, nmv);
-        float2 pr;
-        if (((c >> 1) & 7) < kPolyPairsPer8) {
-          pr = ex2_poly2(x);
-        } else {
-          pr.x = ex2_approx(x.x);
-          pr.y = ex2_approx(x.y);
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int c = half * 64; c < half * 64 + 64; c += 2) {
+          const float2 x = fma2(make_float2(__uint_as_float(s[c >> 5][c & 31]),
+                                            __uint_as_float(s[c >> 5][(c + 1) & 31])),
+                                sl2v, nmv);
+          float2 pr;
+          if (((c >> 1) & 7) < kPolyPairsPer8) {
+            pr = ex2_poly2(x);
+          } else {
+            pr.x = ex2_approx(x.x);
+            pr.y = ex2_approx(x.y);
+          }
+          acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
+          pk[half][(c >> 1) & 31] = pack_half2(pr.x, pr.y);
         }
-        acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
-        pk[c >> 1] = pack_half2(pr.x, pr.y);
+        // First half of P goes to TMEM while the second half is computed.
+        tmem_st32(s_addr + half * 32, pk[half]);
       }
-      tmem_st32(s_addr, pk);  // P over this thread's own (already consumed) S columns
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
-        // is stable; PV_X(j) is not issued before every thread arrives below.
+        // is stable; PV_X(j) is not issued before this thread arrives below.
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
+        for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t o[32];
-          tmem_ld32(o_addr + c2 * 32, o);
+          tmem_ld32(o_addr + c4 * 32, o);
           tmem_ld_wait(o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_addr + c2 * 32, o);
+          tmem_st32(o_addr + c4 * 32, o);
         }
       }
       tmem_st_wait();
@@ -385,22 +387,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       l += a.x + a.y;
     }
     if (ok && nX > 0) {
-      // The row sum is the sum of both halves' partial sums.
-      *slot(nX & 1, half) = l;
-      mbar_arrive(xbar);
-      ok = mbar_wait(xbar, static_cast<uint32_t>(nX & 1), abort_flag, p.status);
-      if (ok) ok = mbar_wait(BAR(kBarODone + X), 0, abort_flag, p.status);
+      ok = mbar_wait(BAR(kBarODone + X), 0, abort_flag, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
-        const float inv_l = 1.f / (l + *slot(nX & 1, half ^ 1));
         tc_fence_after();
+        const float inv_l = 1.f / l;
         __half* orow = p.o + static_cast<long long>(b) * p.o_batch +
                        static_cast<long long>(row) * p.o_tok +
-                       static_cast<long long>(h - p.o_head_base) * p.o_head + half * 64;
+                       static_cast<long long>(h - p.o_head_base) * p.o_head;
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
+        for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t o[32];
-          tmem_ld32(o_addr + c2 * 32, o);
+          tmem_ld32(o_addr + c4 * 32, o);
           tmem_ld_wait(o);
           if (row < p.q_len) {
 #pragma unroll
@@ -410,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
               v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
               v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + c2 * 32 + i * 8) = v;
+              *reinterpret_cast<uint4*>(orow + c4 * 32 + i * 8) = v;
             }
           }
         }
@@ -420,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
