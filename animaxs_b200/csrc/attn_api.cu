@@ -359,6 +359,7 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     jk.weight = static_cast<const __half*>(d->k_norm_weight);
     jk.rows = static_cast<int64_t>(d->batch) * d->kv_len * kv_count;
     np.njobs = 2;
+    np.status = ctx->d_status;
     cudaError_t e = ax::launch_qk_norm(np, stream);
     if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "qk_norm launch");
     qa = qn;
@@ -526,6 +527,7 @@ static int norm_standalone(animaxs_attn_ctx* ctx, const void* in, void* out, con
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(ctx->device);
+  np.status = ctx->d_status;
   cudaError_t e = ax::launch_qk_norm(np, static_cast<cudaStream_t>(stream));
   cudaSetDevice(prev);
   if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "rms norm launch");

@@ -49,6 +49,8 @@ struct NormParams {
   int njobs;
   float eps;
   const float* rope;     // [tokens][64][2][2] or nullptr (no rotation)
+  unsigned int* status;  // device status word (nullable)
+
 };
 
 cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
@@ -57,6 +59,6 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
 
 int attn_fwd_rows_per_cta();  // query rows one attention CTA covers
 
-cudaError_t launch_qk_norm(const NormParams& p, cudaStream_t stream);
+cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
 
 }  // namespace ax
