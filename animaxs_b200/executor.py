@@ -235,16 +235,10 @@ class AttentionExecutor:
                                             _stream_handle(stream))
         self._check(rc)
 
-    def attention(self, q, k, v, out=None, *, causal=False, qk_norm="none", rope_table=None,
-                  q_norm_weight=None, k_norm_weight=None, eps=1e-6, kv_valid_len=None,
-                  kv_valid_lens=None, scale=None, stream=None):
-        """Strided entry: ``q``/``out`` are ``[B, Sq, H, 128]`` and ``k``/``v``
-        ``[B, Sk, Hkv, 128]`` fp16 device tensors with ANY strides (token-major,
-        head-major views, batch gaps).  Enqueues on ``stream`` (default: the
-        current torch stream) and returns ``out``."""
-        import torch
-        if out is None:
-            out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    def strided_desc(self, q, k, v, out, *, causal=False, qk_norm="none", rope_table=None,
+                     q_norm_weight=None, k_norm_weight=None, eps=1e-6, kv_valid_len=None,
+                     kv_valid_lens=None, scale=None) -> AttnDesc:
+        """Descriptor for ``[B, S, H, 128]`` tensors with arbitrary strides (cached)."""
         key = (q.shape, k.shape, q.stride(), k.stride(), v.stride(), out.stride(), causal, qk_norm,
                None if rope_table is None else (rope_table.data_ptr(), rope_table.numel()),
                None if q_norm_weight is None else q_norm_weight.data_ptr(),
@@ -270,6 +264,19 @@ class AttentionExecutor:
             if len(self._desc_cache) > 256:
                 self._desc_cache.clear()
             self._desc_cache[key] = desc
+        return desc
+
+    def attention(self, q, k, v, out=None, *, stream=None, **kw):
+        """Strided entry: ``q``/``out`` are ``[B, Sq, H, 128]`` and ``k``/``v``
+        ``[B, Sk, Hkv, 128]`` fp16 device tensors with ANY strides (token-major,
+        head-major views, batch gaps).  Keywords: ``causal``, ``qk_norm``
+        (``"none"``/``"rms"``/``"rms_rope"``), ``rope_table``, ``q_norm_weight``,
+        ``k_norm_weight``, ``eps``, ``kv_valid_len``, ``kv_valid_lens``, ``scale``.
+        Enqueues on ``stream`` (default: the current torch stream); returns ``out``."""
+        import torch
+        if out is None:
+            out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        desc = self.strided_desc(q, k, v, out, **kw)
         if stream is None:
             stream = torch.cuda.current_stream(q.device)
         rc = self._lib.animaxs_attn_forward(self._ctx, ctypes.byref(desc), q.data_ptr(), k.data_ptr(),

@@ -339,6 +339,75 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
             "steps": steps, "path": "AttentionExecutor.attention -> animaxs_attn_forward (fused rms/rope)"}
 
 
+def run_cfg5(args, rank, world, local_rank):
+    """Config 5: 16384-token DiT self-attention (rms + 3-D RoPE 1x128x128), 16
+    heads sharded over the ranks, one NCCL all-gather of the [16384, 2048] fp16
+    output; every rank ends with the full output.  value = calls/s."""
+    import torch
+    import torch.distributed as dist
+
+    import animaxs_b200 as ax
+    from animaxs_b200.sharded import HeadShardedAttention, share_unique_id
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ex = ax.AttentionExecutor(local_rank)
+    if world > 1:
+        uid = share_unique_id()
+    else:
+        from animaxs_b200.sharded import nccl_unique_id
+        uid = nccl_unique_id()
+    sh = HeadShardedAttention(ex, rank, world, uid)
+    s_len = 16384
+    g = torch.Generator(device=device).manual_seed(0)
+    q, k, v = (torch.randn(1, s_len, HEADS, HD, generator=g, device=device).half() for _ in range(3))
+    rope = torch.from_numpy(ax.DitRoPE.generate(1, 128, 128).reshape(s_len, 64, 2, 2)).to(device)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        sh(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope, stream=stream)
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        sh(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope, stream=stream)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ex.synchronize(stream)
+    el = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([el], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    flops = 4.0 * s_len * s_len * HD * HEADS
+    sh.close()
+    if rank != 0:
+        return
+    peak_burst, peak_sust, _, peak_kind = peaks()
+    tf = flops * args.steps / (el / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "config-5 DiT self-attention, 16384 tokens, heads sharded + NCCL all-gather",
+        "value": args.steps / (el / 1e3), "unit": "calls/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": "config5: S=16384, 16 heads x 128, rms + rope3d(1,128,128)",
+                   "parallelism": f"heads/{world} + all-gather"},
+        "tflops_total": tf, "tflops_per_gpu": tf / world,
+        "frac_of_sustained_peak_per_gpu": tf / world / peak_sust, "peak_kind": peak_kind,
+        "clocks": clocks}), flush=True)
+
+
 def profile_kernel(args):
     import torch
 
@@ -364,6 +433,9 @@ def main():
     ap.add_argument("--impl", default="animaxs", choices=["animaxs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5"],
+                    help="cfg4 (default): the 8-step DiT workload, batch-sharded; cfg5: the "
+                         "16384-token self-attention, heads sharded + one NCCL all-gather")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only run the fused rms+rope3d self-attention (prologue + flash kernel) "
                          "on a batch-4 4096-token case (192 MiB of inputs, > L2): the small "
@@ -387,7 +459,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_gpu(args, rank, world, local_rank)
+        if args.workload == "cfg5":
+            run_cfg5(args, rank, world, local_rank)
+        else:
+            run_gpu(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
