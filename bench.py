@@ -46,6 +46,10 @@ CROSS_FLOPS = 4.0 * S_SELF * S_CTX * HD * HEADS   # 17.2 GFLOP per cross-attenti
 IMAGE_FLOPS = CALLS_PER_IMAGE * (SELF_FLOPS + CROSS_FLOPS)
 BATCH = 8                                         # images per GPU per step (config 4)
 POOL_BLOCKS = 3                                   # distinct resident input sets (> L2)
+# DRAM bytes (read + write) of one batch-8 self-attention flash launch: the ncu
+# capture in profiles/attn_fwd_sm100_selfattn4096_batch4.md measured 250.2 MB
+# for batch 4; traffic scales with the batch.
+TRAFFIC_PER_LAUNCH_MB = 500.4
 
 METRIC = ("DiT attention throughput, 8-step 1024x1024 workload "
           "(28 blocks x 8 steps x [4096-tok self rms+rope3d + 4096x512 cross rms])")
@@ -254,7 +258,8 @@ def run_gpu(args, rank, world, local_rank):
                      "frac_of_burst_peak": achieved / peak_burst,
                      "flops_per_launch": BATCH * SELF_FLOPS, "avg_launch_ms": avg_kern,
                      "max_launch_ms": kern_max_ms, "launches_timed": n_kern,
-                     "traffic": None},
+                     "traffic": TRAFFIC_PER_LAUNCH_MB * 1e6, "traffic_unit": "bytes per launch",
+                     "algorithmic_bytes": BATCH * 4 * S_SELF * HEADS * HD * 2},
         "clocks": clocks,
         "gpu_launches": launches,
         "e2e": e2e,
