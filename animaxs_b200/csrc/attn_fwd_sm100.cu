@@ -19,14 +19,17 @@
 //   warp 8     MMA issuer + TMEM owner: S_X = Q_X K_j^T (tcgen05.mma kind::f16,
 //              both operands in shared memory) and O_X += P_X V_j with P read
 //              straight from TMEM (A operand in TMEM).
-//   warp 9     TMA producer: both Q tiles once, then K_j / V_j into 2-stage rings.
+//   warp 9     TMA producer: both Q tiles once, then K_j / V_j into 2-stage
+//              rings, in the order the MMA warp consumes them.
 //   warps 10-11 idle (they complete the third warpgroup for setmaxnreg).
 // TMEM (512 columns): S_A [0,128), S_B [128,256) (P_X overlays the first 64
 // columns of S_X), O_A [256,384), O_B [384,512).
 //
 // The tensor core alternates PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): while one
 // softmax warpgroup works on its tile, the tensor core runs the other tile's
-// MMAs.  tcgen05.mma ops from one thread execute in issue order, which is what
+// MMAs.  P is published in two halves (keys 0-63, 64-127) and PV is issued in
+// the matching two halves, so the first half of PV runs while the softmax is
+// still computing the second half of P.  tcgen05.mma ops from one thread execute in issue order, which is what
 // lets QK_X(j+1) overwrite the TMEM columns PV_X(j) reads P_X(j) from.
 #include <atomic>
 
@@ -39,24 +42,31 @@ namespace {
 constexpr uint32_t kTileBytes = kTileM * kHeadDim * 2;  // 32 KiB: one 128x128 fp16 tile
 constexpr uint32_t kPanelBytes = 128 * 128;             // 128 rows x 128 B (64 fp16)
 constexpr uint32_t kSmQ = 0;                            // Q_A, Q_B
-constexpr uint32_t kSmK = kSmQ + 2 * kTileBytes;        // 2 stages
-constexpr uint32_t kSmV = kSmK + 2 * kTileBytes;        // 2 stages
-constexpr uint32_t kSmBar = kSmV + 2 * kTileBytes;
+// Ring depths.  A tile load measured ~4000 cycles from issue to arrival under
+// full load; two stages each cover it (a third V stage, which still fits in
+// 227 KiB, measured no faster).
+constexpr int kKStages = 2;
+constexpr int kVStages = 2;
+constexpr uint32_t kSmK = kSmQ + 2 * kTileBytes;
+constexpr uint32_t kSmV = kSmK + kKStages * kTileBytes;
+constexpr uint32_t kSmBar = kSmV + kVStages * kTileBytes;
 constexpr uint32_t kSmemBytes = kSmBar + 256 + 1024;    // + barriers + alignment slack
 constexpr int kThreads = 384;  // warpgroups: softmax A, softmax B, MMA/TMA (+2 idle warps)
 
 enum : int {
   kBarQ = 0,
-  kBarKFull = 1,   // +stage
-  kBarKEmpty = 3,  // +stage
-  kBarVFull = 5,   // +stage
-  kBarVEmpty = 7,  // +stage
-  kBarSFull = 9,   // +tile
-  kBarPFull = 11,  // +tile (128 arrivals)
-  kBarODone = 13,  // +tile
-  kBarDone = 15,
-  kNumBars = 16
+  kBarKFull = 1,                         // +stage
+  kBarKEmpty = kBarKFull + kKStages,     // +stage
+  kBarVFull = kBarKEmpty + kKStages,     // +stage
+  kBarVEmpty = kBarVFull + kVStages,     // +stage
+  kBarSFull = kBarVEmpty + kVStages,     // +tile
+  kBarPHalf = kBarSFull + 2,  // +2*tile + half (128 arrivals): P for keys [64*half, 64*half+64) in TMEM
+  kBarODone = kBarPHalf + 4,  // +tile
+  kBarDone = kBarODone + 2,
+  kNumBars = kBarDone + 1
 };
+static_assert(kNumBars * 8 + 8 <= 256, "barrier block overflows its 256 bytes");
+static_assert(kSmBar + 256 + 1024 <= 227 * 1024, "shared memory exceeds the 227 KiB opt-in");
 constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 
@@ -116,23 +126,26 @@ __device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile, int kk) {
 
 // Descriptors advance by constant offsets of their start-address field
 // (bits 0-13, address >> 4; every operand lies below 256 KiB of shared memory,
-// so the field never carries).  The loops are unrolled: the MMA thread's issue
-// latency sits on the critical path whenever the tensor core waits for PV.
+// so the field never carries).  The loops are unrolled and run on the whole MMA
+// warp (one elected lane issues): the issue rate sits on the critical path.
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint32_t k_tile) {
   const uint64_t a0 = kmajor_desc(q_tile, 0), b0 = kmajor_desc(k_tile, 0);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
     const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4);
-    umma_f16_ss(d_tmem, a0 + off, b0 + off, kIdescQK, kk > 0 ? 1u : 0u);
+    umma_f16_ss_warp(d_tmem, a0 + off, b0 + off, kIdescQK, kk > 0 ? 1u : 0u);
   }
 }
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
-                                         bool accumulate) {
+// Half `hf` of O (+)= P V: k-steps 4*hf .. 4*hf+3 (keys [64*hf, 64*hf+64)).
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
+                                              int hf, bool accumulate) {
   const uint64_t b0 = vmajor_desc(v_tile, 0);
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
-    umma_f16_ts(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
+  for (int k4 = 0; k4 < 4; ++k4) {
+    const int kk = hf * 4 + k4;
+    umma_f16_ts_warp(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
                 (accumulate || kk > 0) ? 1u : 0u);
+  }
 }
 
 __device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, int causal) {
@@ -174,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(BAR(i), (i == kBarPFull || i == kBarPFull + 1) ? 128u : 1u);
+      mbar_init(BAR(i), (i >= kBarPHalf && i < kBarPHalf + 4) ? 128u : 1u);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -197,97 +210,112 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 9) {
     // ------------------------------------------------------------ producer --
     if (lane == 0 && n_kv > 0) {
-      int armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
+      int armed_k[kKStages] = {}, armed_v[kVStages] = {};
       mbar_arrive_expect_tx(BAR(kBarQ), 2 * kTileBytes);
       tma_load_4d(sQ, &tm_q, BAR(kBarQ), 0, q0, h, b);
       tma_load_4d(sQ + kPanelBytes, &tm_q, BAR(kBarQ), 64, q0, h, b);
       tma_load_4d(sQ + kTileBytes, &tm_q, BAR(kBarQ), 0, q0 + kTileM, h, b);
       tma_load_4d(sQ + kTileBytes + kPanelBytes, &tm_q, BAR(kBarQ), 64, q0 + kTileM, h, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(BAR(kBarKEmpty + st), ph ^ 1u, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(BAR(kBarKFull + st), kTileBytes);
-        tma_load_4d(sK + st * kTileBytes, &tm_k, BAR(kBarKFull + st), 0, j * kTileN, kvh, b);
-        tma_load_4d(sK + st * kTileBytes + kPanelBytes, &tm_k, BAR(kBarKFull + st), 64,
-                    j * kTileN, kvh, b);
-        ++armed_k[st];
-        if (!mbar_wait(BAR(kBarVEmpty + st), ph ^ 1u, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(BAR(kBarVFull + st), kTileBytes);
-        tma_load_4d(sV + st * kTileBytes, &tm_v, BAR(kBarVFull + st), 0, j * kTileN, kvh, b);
-        tma_load_4d(sV + st * kTileBytes + kPanelBytes, &tm_v, BAR(kBarVFull + st), 64,
-                    j * kTileN, kvh, b);
-        ++armed_v[st];
+      // Loads in the order the MMA warp consumes them: K_0, then V_j, K_{j+1}.
+      // Tile j of a ring with n stages lives in stage j % n; the wait for a
+      // free stage is on the phase its previous occupant's release completed.
+      auto load = [&](bool is_k, int j) -> bool {
+        const int nst = is_k ? kKStages : kVStages;
+        const int st = j % nst;
+        const uint32_t ph = static_cast<uint32_t>(j / nst) & 1u;
+        const uint32_t full = BAR((is_k ? kBarKFull : kBarVFull) + st);
+        const uint32_t dst = (is_k ? sK : sV) + st * kTileBytes;
+        const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+        if (!mbar_wait(BAR((is_k ? kBarKEmpty : kBarVEmpty) + st), ph ^ 1u, abort_flag, p.status))
+          return false;
+        mbar_arrive_expect_tx(full, kTileBytes);
+        tma_load_4d(dst, tm, full, 0, j * kTileN, kvh, b);
+        tma_load_4d(dst + kPanelBytes, tm, full, 64, j * kTileN, kvh, b);
+        ++(is_k ? armed_k[st] : armed_v[st]);
+        return true;
+      };
+      if (load(true, 0)) {
+        for (int j = 0; j < n_kv; ++j) {
+          if (!load(false, j)) break;
+          if (j + 1 < n_kv && !load(true, j + 1)) break;
+        }
       }
       // Never leave the CTA with a tensor copy still landing in shared memory:
       // wait (bounded, ignoring the abort flag) for every phase armed above.
-      int local_abort = 0;
-      mbar_wait(BAR(kBarQ), 0, &local_abort, nullptr);
-      for (int st = 0; st < 2; ++st) {
-        local_abort = 0;
-        if (armed_k[st]) mbar_wait(BAR(kBarKFull + st), (armed_k[st] - 1) & 1, &local_abort, nullptr);
-        local_abort = 0;
-        if (armed_v[st]) mbar_wait(BAR(kBarVFull + st), (armed_v[st] - 1) & 1, &local_abort, nullptr);
-      }
+      mbar_wait_drain(BAR(kBarQ), 0);
+      for (int st = 0; st < kKStages; ++st)
+        if (armed_k[st]) mbar_wait_drain(BAR(kBarKFull + st), (armed_k[st] - 1) & 1);
+      for (int st = 0; st < kVStages; ++st)
+        if (armed_v[st]) mbar_wait_drain(BAR(kBarVFull + st), (armed_v[st] - 1) & 1);
     }
   } else if (warp == 8) {
     // ----------------------------------------------------------------- MMA --
-    if (lane == 0 && n_kv > 0) {
+    // The whole warp runs this loop (waits, address arithmetic); one elected
+    // lane issues each MMA and commit.
+    if (n_kv > 0) {
       const uint32_t sQA = sQ, sQB = sQ + kTileBytes;
-      bool ok = mbar_wait(BAR(kBarQ), 0, abort_flag, p.status);
-      if (ok) ok = mbar_wait(BAR(kBarKFull + 0), 0, abort_flag, p.status);
+      bool ok = mbar_wait_warp(BAR(kBarQ), 0, abort_flag, p.status);
+      if (ok) ok = mbar_wait_warp(BAR(kBarKFull + 0), 0, abort_flag, p.status);
       tc_fence_after();
       if (ok) {
         if (nA > 0) {
           issue_qk(tmem + 0, sQA, sK);
-          tc_commit(BAR(kBarSFull + 0));
+          tc_commit_warp(BAR(kBarSFull + 0));
         }
         if (nB > 0) {
           issue_qk(tmem + 128, sQB, sK);
-          tc_commit(BAR(kBarSFull + 1));
+          tc_commit_warp(BAR(kBarSFull + 1));
         }
-        tc_commit(BAR(kBarKEmpty + 0));
+        tc_commit_warp(BAR(kBarKEmpty + 0));
       }
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int vst = j % kVStages;
+        const uint32_t vph = static_cast<uint32_t>(j / kVStages) & 1u;
         const int j1 = j + 1;
-        const int st1 = j1 & 1;
-        const uint32_t ph1 = (j1 >> 1) & 1;
-        const uint32_t vt = sV + st * kTileBytes;
+        const int st1 = j1 % kKStages;
+        const uint32_t ph1 = static_cast<uint32_t>(j1 / kKStages) & 1u;
+        const uint32_t vt = sV + vst * kTileBytes;
         const uint32_t kt1 = sK + st1 * kTileBytes;
-        if (!mbar_wait(BAR(kBarVFull + st), ph, abort_flag, p.status)) break;
+        if (!mbar_wait_warp(BAR(kBarVFull + vst), vph, abort_flag, p.status)) break;
         if (j < nA) {
-          if (!mbar_wait(BAR(kBarPFull + 0), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          if (!mbar_wait_warp(BAR(kBarPHalf + 0), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
           tc_fence_after();
-          issue_pv(tmem + kColO, tmem + 0, vt, j > 0);
-          if (j == nA - 1) tc_commit(BAR(kBarODone + 0));
+          issue_pv_half(tmem + kColO, tmem + 0, vt, 0, j > 0);
+          if (!mbar_wait_warp(BAR(kBarPHalf + 1), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          tc_fence_after();
+          issue_pv_half(tmem + kColO, tmem + 0, vt, 1, true);
+          if (j == nA - 1) tc_commit_warp(BAR(kBarODone + 0));
         }
         if (j1 < n_kv) {
-          if (!mbar_wait(BAR(kBarKFull + st1), ph1, abort_flag, p.status)) break;
+          if (!mbar_wait_warp(BAR(kBarKFull + st1), ph1, abort_flag, p.status)) break;
           tc_fence_after();
         }
         if (j1 < nA) {
           issue_qk(tmem + 0, sQA, kt1);
-          tc_commit(BAR(kBarSFull + 0));
+          tc_commit_warp(BAR(kBarSFull + 0));
         }
         if (j < nB) {
-          if (!mbar_wait(BAR(kBarPFull + 1), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          if (!mbar_wait_warp(BAR(kBarPHalf + 2), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
           tc_fence_after();
-          issue_pv(tmem + kColO + 128, tmem + 128, vt, j > 0);
-          if (j == nB - 1) tc_commit(BAR(kBarODone + 1));
+          issue_pv_half(tmem + kColO + 128, tmem + 128, vt, 0, j > 0);
+          if (!mbar_wait_warp(BAR(kBarPHalf + 3), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          tc_fence_after();
+          issue_pv_half(tmem + kColO + 128, tmem + 128, vt, 1, true);
+          if (j == nB - 1) tc_commit_warp(BAR(kBarODone + 1));
         }
+        // V_j's last reader has been issued: release its stage now (the commit
+        // fires when PV_B(j) retires), not after QK_B(j+1).
+        tc_commit_warp(BAR(kBarVEmpty + vst));
         if (j1 < nB) {
           issue_qk(tmem + 128, sQB, kt1);
-          tc_commit(BAR(kBarSFull + 1));
+          tc_commit_warp(BAR(kBarSFull + 1));
         }
-        if (j1 < n_kv) tc_commit(BAR(kBarKEmpty + st1));
-        tc_commit(BAR(kBarVEmpty + st));
+        if (j1 < n_kv) tc_commit_warp(BAR(kBarKEmpty + st1));
       }
-      // All MMAs this thread issued must retire before TMEM is released.
-      tc_commit(BAR(kBarDone));
-      int local_abort = 0;
-      mbar_wait(BAR(kBarDone), 0, &local_abort, nullptr);
+      // All MMAs this warp issued must retire before TMEM is released.
+      tc_commit_warp(BAR(kBarDone));
+      mbar_wait_drain(BAR(kBarDone), 0);
+      __syncwarp();
     }
   }
   } else {
@@ -325,20 +353,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (key0 + c >= lim) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      // Row max with 8 independent chains.
+      // Row max: 8 independent chains of three-input max over 16 values each.
+#define SV(c) __uint_as_float(s[(c) >> 5][(c) & 31])
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(s[0][i]);
+      for (int i = 0; i < 8; ++i) {
+        mx[i] = fmax3(SV(i), SV(i + 8), SV(i + 16));
 #pragma unroll
-      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(s[c >> 5][c & 31]));
-      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+        for (int c = 24; c < 120; c += 16) mx[i] = fmax3(mx[i], SV(c + i), SV(c + 8 + i));
+        mx[i] = fmaxf(mx[i], SV(120 + i));
+      }
+#undef SV
+      const float tmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                               fmaxf(mx[6], mx[7])) * sl2;
       const float m_new = fmaxf(m, tmax);
       const bool grow = m_new > m + kRescaleThreshold;  // also true on the first tile
       const float alpha = grow ? ex2_approx(m - m_new) : 1.f;  // 0 on the first tile (m = -inf)
       if (grow) {
         l *= alpha;
         m = m_new;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
+        // is stable; PV_X(j) starts only after this thread's first arrival below.
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c4 * 32, o);
+          tmem_ld_wait(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_addr + c4 * 32, o);
+        }
       }
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
       const float2 sl2v = make_float2(sl2, sl2);
@@ -363,25 +409,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
           pk[half][(c >> 1) & 31] = pack_half2(pr.x, pr.y);
         }
-        // First half of P goes to TMEM while the second half is computed.
+        // Publish this half of P: the MMA warp starts its half of PV_X(j) while
+        // the second half is still being computed.
         tmem_st32(s_addr + half * 32, pk[half]);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(BAR(kBarPHalf + 2 * X + half));
       }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
-        // is stable; PV_X(j) is not issued before this thread arrives below.
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c4 * 32, o);
-          tmem_ld_wait(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_addr + c4 * 32, o);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(BAR(kBarPFull + X));
       const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
       const float2 a = add2(a01, a23);
       l += a.x + a.y;

@@ -80,6 +80,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Wait bounded by time only (the abort flag is ignored): used where in-flight
+// asynchronous work must drain before its resources are released.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++n & 15u) == 0 && globaltimer_ns() - t0 > ANIMAXS_WAIT_TIMEOUT_NS) return false;
+  }
+}
+
+// mbar_wait for a whole converged warp: every lane polls, and lane 0's outcome
+// is returned to all so that the warp leaves together.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, uint32_t* status) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, (lane_id() == 0) ? status : nullptr);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 // --------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
@@ -151,6 +171,43 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Warp-wide forms: every lane of a converged warp executes the call and one
+// lane, picked by elect.sync, issues the instruction.  Running the issuing
+// loop on the whole warp (instead of inside a one-lane branch) keeps its
+// address arithmetic warp-uniform; measured on B200 with FMA-heavy warps on
+// the same scheduler, the one-lane loop issued a 128x128x16 MMA every ~104
+// cycles and the warp-wide loop every ~70 (the MMA itself takes 64).
+__device__ __forceinline__ void umma_f16_ss_warp(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %4, 0;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %4, 0;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_warp(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand.
 //   bits  0-13 start address >> 4, 16-29 leading byte offset >> 4,
 //   32-45 stride byte offset >> 4, 46-47 version (1 on sm_100),
@@ -217,6 +274,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Three-input max (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
