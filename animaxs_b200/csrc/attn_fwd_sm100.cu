@@ -7,8 +7,14 @@
 // Same math: O = softmax(Q K^T * scale + mask) V with fp32 softmax statistics,
 // computed as an online (flash) softmax over 128-key tiles.
 //
-// One CTA = two 128-row query tiles (A: rows q0..q0+127, B: q0+128..q0+255) of
-// one (batch, head); both stream the same K/V tiles.  Twelve warps:
+// Persistent: one CTA per SM loops over work items; an item is two 128-row
+// query tiles (A: rows q0..q0+127, B: q0+128..q0+255) of one (batch, head),
+// both streaming the same K/V tiles.  Items are dealt round-robin (item w to
+// CTA w % gridDim.x).  The producer loads the next item's Q, K and V while the
+// current item drains, and the next item's first QK runs while the softmax
+// warps still store the current item's O, so the per-item start-up (Q load,
+// first QK) and epilogue -- measured ~6.5 us per 256-row CTA when every item
+// was its own CTA -- overlap with work.  Twelve warps:
 //   warps 0-3  softmax for tile A, warps 4-7 softmax for tile B: thread t owns
 //              query row t of its tile (= TMEM lane t).  Per K/V tile it reads
 //              S from TMEM, applies the causal / key-padding masks, updates the
@@ -29,8 +35,10 @@
 // softmax warpgroup works on its tile, the tensor core runs the other tile's
 // MMAs.  P is published in two halves (keys 0-63, 64-127) and PV is issued in
 // the matching two halves, so the first half of PV runs while the softmax is
-// still computing the second half of P.  tcgen05.mma ops from one thread execute in issue order, which is what
-// lets QK_X(j+1) overwrite the TMEM columns PV_X(j) reads P_X(j) from.
+// still computing the second half of P.  tcgen05.mma ops from one thread
+// execute in issue order, which is what lets QK_X(j+1) overwrite the TMEM
+// columns PV_X(j) reads P_X(j) from.  Barrier phases count tiles and items
+// across the whole persistent loop.
 #include <atomic>
 
 #include "kernels.h"
@@ -61,8 +69,9 @@ enum : int {
   kBarVEmpty = kBarVFull + kVStages,     // +stage
   kBarSFull = kBarVEmpty + kVStages,     // +tile
   kBarPHalf = kBarSFull + 2,  // +2*tile + half (128 arrivals): P for keys [64*half, 64*half+64) in TMEM
-  kBarODone = kBarPHalf + 4,  // +tile
-  kBarDone = kBarODone + 2,
+  kBarODone = kBarPHalf + 4,  // +tile: the item's last PV_X retired
+  kBarQFree = kBarODone + 2,  // the item's last QK retired: Q may be reloaded
+  kBarDone = kBarQFree + 1,
   kNumBars = kBarDone + 1
 };
 static_assert(kNumBars * 8 + 8 <= 256, "barrier block overflows its 256 bytes");
@@ -171,19 +180,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int pair = p.causal ? (p.n_q_tiles - 1 - static_cast<int>(blockIdx.x))
-                            : static_cast<int>(blockIdx.x);
-  const int h = p.head_offset + static_cast<int>(blockIdx.y);
-  const int b = static_cast<int>(blockIdx.z);
-  const int kvh = h / p.heads_per_kv;
-  const int q0 = pair * 2 * kTileM;
-
-  int valid = p.kv_valid;
-  if (p.kv_valid_dev != nullptr) valid = p.kv_valid_dev[b];
-  valid = min(max(valid, 1), p.kv_len);
-  const int nA = kv_tiles_for(q0, p.q_len, valid, p.causal);
-  const int nB = kv_tiles_for(q0 + kTileM, p.q_len, valid, p.causal);
-  const int n_kv = max(nA, nB);
+  // Work item w -> (query-tile pair, head, batch); causal launches take the
+  // longest pairs (the last ones) first.
+  struct Item {
+    int q0, h, b, kvh, valid, nA, nB, n_kv;
+  };
+  auto item_of = [&](int w) {
+    Item it;
+    const int pi = w % p.n_q_tiles;
+    const int hb = w / p.n_q_tiles;
+    const int pair = p.causal ? (p.n_q_tiles - 1 - pi) : pi;
+    it.h = p.head_offset + hb % p.heads_in_launch;
+    it.b = hb / p.heads_in_launch;
+    it.kvh = it.h / p.heads_per_kv;
+    it.q0 = pair * 2 * kTileM;
+    int valid = p.kv_valid;
+    if (p.kv_valid_dev != nullptr) valid = p.kv_valid_dev[it.b];
+    it.valid = min(max(valid, 1), p.kv_len);
+    it.nA = kv_tiles_for(it.q0, p.q_len, it.valid, p.causal);
+    it.nB = kv_tiles_for(it.q0 + kTileM, p.q_len, it.valid, p.causal);
+    it.n_kv = max(it.nA, it.nB);
+    return it;
+  };
+  const int w0 = static_cast<int>(blockIdx.x);
+  const int wstep = static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
@@ -209,40 +229,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(AX_OTHER_REGS));
   if (warp == 9) {
     // ------------------------------------------------------------ producer --
-    if (lane == 0 && n_kv > 0) {
-      int armed_k[kKStages] = {}, armed_v[kVStages] = {};
-      mbar_arrive_expect_tx(BAR(kBarQ), 2 * kTileBytes);
-      tma_load_4d(sQ, &tm_q, BAR(kBarQ), 0, q0, h, b);
-      tma_load_4d(sQ + kPanelBytes, &tm_q, BAR(kBarQ), 64, q0, h, b);
-      tma_load_4d(sQ + kTileBytes, &tm_q, BAR(kBarQ), 0, q0 + kTileM, h, b);
-      tma_load_4d(sQ + kTileBytes + kPanelBytes, &tm_q, BAR(kBarQ), 64, q0 + kTileM, h, b);
-      // Loads in the order the MMA warp consumes them: K_0, then V_j, K_{j+1}.
-      // Tile j of a ring with n stages lives in stage j % n; the wait for a
-      // free stage is on the phase its previous occupant's release completed.
-      auto load = [&](bool is_k, int j) -> bool {
-        const int nst = is_k ? kKStages : kVStages;
-        const int st = j % nst;
-        const uint32_t ph = static_cast<uint32_t>(j / nst) & 1u;
+    if (lane == 0) {
+      int armed_q = 0, armed_k[kKStages] = {}, armed_v[kVStages] = {};
+      uint32_t gk = 0, gv = 0;  // K / V tiles loaded so far (ring position)
+      // Tile number g of a ring with n stages lives in stage g % n; the wait for
+      // a free stage is on the phase its previous occupant's release completed.
+      auto load = [&](bool is_k, uint32_t g, int row0, int kvh, int b) -> bool {
+        const uint32_t nst = is_k ? kKStages : kVStages;
+        const uint32_t st = g % nst;
+        const uint32_t ph = (g / nst) & 1u;
         const uint32_t full = BAR((is_k ? kBarKFull : kBarVFull) + st);
         const uint32_t dst = (is_k ? sK : sV) + st * kTileBytes;
         const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
         if (!mbar_wait(BAR((is_k ? kBarKEmpty : kBarVEmpty) + st), ph ^ 1u, abort_flag, p.status))
           return false;
         mbar_arrive_expect_tx(full, kTileBytes);
-        tma_load_4d(dst, tm, full, 0, j * kTileN, kvh, b);
-        tma_load_4d(dst + kPanelBytes, tm, full, 64, j * kTileN, kvh, b);
+        tma_load_4d(dst, tm, full, 0, row0, kvh, b);
+        tma_load_4d(dst + kPanelBytes, tm, full, 64, row0, kvh, b);
         ++(is_k ? armed_k[st] : armed_v[st]);
         return true;
       };
-      if (load(true, 0)) {
-        for (int j = 0; j < n_kv; ++j) {
-          if (!load(false, j)) break;
-          if (j + 1 < n_kv && !load(true, j + 1)) break;
+      bool ok = true;
+      int it = 0;
+      for (int w = w0; ok && w < p.n_items; w += wstep, ++it) {
+        const Item I = item_of(w);
+        // Q is reloaded once the previous item's last QK has retired.
+        if (it > 0 && !(ok = mbar_wait(BAR(kBarQFree), static_cast<uint32_t>((it - 1) & 1),
+                                       abort_flag, p.status)))
+          break;
+        mbar_arrive_expect_tx(BAR(kBarQ), 2 * kTileBytes);
+        tma_load_4d(sQ, &tm_q, BAR(kBarQ), 0, I.q0, I.h, I.b);
+        tma_load_4d(sQ + kPanelBytes, &tm_q, BAR(kBarQ), 64, I.q0, I.h, I.b);
+        tma_load_4d(sQ + kTileBytes, &tm_q, BAR(kBarQ), 0, I.q0 + kTileM, I.h, I.b);
+        tma_load_4d(sQ + kTileBytes + kPanelBytes, &tm_q, BAR(kBarQ), 64, I.q0 + kTileM, I.h, I.b);
+        ++armed_q;
+        // K/V in the order the MMA warp consumes them: K_0, then V_j, K_{j+1}.
+        if (!(ok = load(true, gk++, 0, I.kvh, I.b))) break;
+        for (int j = 0; ok && j < I.n_kv; ++j) {
+          if (!(ok = load(false, gv++, j * kTileN, I.kvh, I.b))) break;
+          if (j + 1 < I.n_kv && !(ok = load(true, gk++, (j + 1) * kTileN, I.kvh, I.b))) break;
         }
       }
       // Never leave the CTA with a tensor copy still landing in shared memory:
       // wait (bounded, ignoring the abort flag) for every phase armed above.
-      mbar_wait_drain(BAR(kBarQ), 0);
+      if (armed_q) mbar_wait_drain(BAR(kBarQ), (armed_q - 1) & 1);
       for (int st = 0; st < kKStages; ++st)
         if (armed_k[st]) mbar_wait_drain(BAR(kBarKFull + st), (armed_k[st] - 1) & 1);
       for (int st = 0; st < kVStages; ++st)
@@ -252,42 +282,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------------- MMA --
     // The whole warp runs this loop (waits, address arithmetic); one elected
     // lane issues each MMA and commit.
-    if (n_kv > 0) {
-      const uint32_t sQA = sQ, sQB = sQ + kTileBytes;
-      bool ok = mbar_wait_warp(BAR(kBarQ), 0, abort_flag, p.status);
-      if (ok) ok = mbar_wait_warp(BAR(kBarKFull + 0), 0, abort_flag, p.status);
+    const uint32_t sQA = sQ, sQB = sQ + kTileBytes;
+    // Running counters (unsigned: ring stage and phase are bit operations).
+    uint32_t gk = 0, gv = 0;  // K / V tiles consumed so far
+    uint32_t tA = 0, tB = 0;  // tiles of A / B in earlier items (PHalf phases)
+    bool ok = true;
+    uint32_t it = 0;
+    auto k_full = [&](uint32_t g) {
+      return mbar_wait_warp(BAR(kBarKFull + g % kKStages), (g / kKStages) & 1u, abort_flag, p.status);
+    };
+    for (int w = w0; ok && w < p.n_items; w += wstep, ++it) {
+      const Item I = item_of(w);
+      const int nA = I.nA, nB = I.nB, n_kv = I.n_kv;
+      if (!(ok = mbar_wait_warp(BAR(kBarQ), it & 1u, abort_flag, p.status))) break;
+      if (!(ok = k_full(gk))) break;
       tc_fence_after();
-      if (ok) {
-        if (nA > 0) {
-          issue_qk(tmem + 0, sQA, sK);
-          tc_commit_warp(BAR(kBarSFull + 0));
-        }
-        if (nB > 0) {
-          issue_qk(tmem + 128, sQB, sK);
-          tc_commit_warp(BAR(kBarSFull + 1));
-        }
-        tc_commit_warp(BAR(kBarKEmpty + 0));
+      const uint32_t k0 = sK + (gk % kKStages) * kTileBytes;
+      if (nA > 0) {
+        issue_qk(tmem + 0, sQA, k0);
+        tc_commit_warp(BAR(kBarSFull + 0));
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int vst = j % kVStages;
-        const uint32_t vph = static_cast<uint32_t>(j / kVStages) & 1u;
+      if (nB > 0) {
+        issue_qk(tmem + 128, sQB, k0);
+        tc_commit_warp(BAR(kBarSFull + 1));
+      }
+      tc_commit_warp(BAR(kBarKEmpty + gk % kKStages));
+      ++gk;
+      if (n_kv == 1) tc_commit_warp(BAR(kBarQFree));  // the item's last QK
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t vst = gv % kVStages;
+        const uint32_t vph = (gv / kVStages) & 1u;
         const int j1 = j + 1;
-        const int st1 = j1 % kKStages;
-        const uint32_t ph1 = static_cast<uint32_t>(j1 / kKStages) & 1u;
         const uint32_t vt = sV + vst * kTileBytes;
-        const uint32_t kt1 = sK + st1 * kTileBytes;
-        if (!mbar_wait_warp(BAR(kBarVFull + vst), vph, abort_flag, p.status)) break;
+        const uint32_t kt1 = sK + (gk % kKStages) * kTileBytes;
+        if (!(ok = mbar_wait_warp(BAR(kBarVFull + vst), vph, abort_flag, p.status))) break;
         if (j < nA) {
-          if (!mbar_wait_warp(BAR(kBarPHalf + 0), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          // An item's first PV overwrites O_A.  The softmax threads publish the
+          // item's first P only after their previous epilogue has read O_A out
+          // of TMEM, so the PHalf wait below also orders that.
+          const uint32_t pph = (tA + j) & 1u;
+          if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 0), pph, abort_flag, p.status))) break;
           tc_fence_after();
           issue_pv_half(tmem + kColO, tmem + 0, vt, 0, j > 0);
-          if (!mbar_wait_warp(BAR(kBarPHalf + 1), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 1), pph, abort_flag, p.status))) break;
           tc_fence_after();
           issue_pv_half(tmem + kColO, tmem + 0, vt, 1, true);
           if (j == nA - 1) tc_commit_warp(BAR(kBarODone + 0));
         }
         if (j1 < n_kv) {
-          if (!mbar_wait_warp(BAR(kBarKFull + st1), ph1, abort_flag, p.status)) break;
+          if (!(ok = k_full(gk))) break;
           tc_fence_after();
         }
         if (j1 < nA) {
@@ -295,10 +338,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit_warp(BAR(kBarSFull + 0));
         }
         if (j < nB) {
-          if (!mbar_wait_warp(BAR(kBarPHalf + 2), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          const uint32_t pph = (tB + j) & 1u;
+          if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 2), pph, abort_flag, p.status))) break;
           tc_fence_after();
           issue_pv_half(tmem + kColO + 128, tmem + 128, vt, 0, j > 0);
-          if (!mbar_wait_warp(BAR(kBarPHalf + 3), static_cast<uint32_t>(j & 1), abort_flag, p.status)) break;
+          if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 3), pph, abort_flag, p.status))) break;
           tc_fence_after();
           issue_pv_half(tmem + kColO + 128, tmem + 128, vt, 1, true);
           if (j == nB - 1) tc_commit_warp(BAR(kBarODone + 1));
@@ -306,147 +350,162 @@ __global__ void __launch_bounds__(kThreads, 1)
         // V_j's last reader has been issued: release its stage now (the commit
         // fires when PV_B(j) retires), not after QK_B(j+1).
         tc_commit_warp(BAR(kBarVEmpty + vst));
+        ++gv;
         if (j1 < nB) {
           issue_qk(tmem + 128, sQB, kt1);
           tc_commit_warp(BAR(kBarSFull + 1));
         }
-        if (j1 < n_kv) tc_commit_warp(BAR(kBarKEmpty + st1));
+        if (j1 < n_kv) {
+          tc_commit_warp(BAR(kBarKEmpty + gk % kKStages));
+          ++gk;
+          if (j1 == n_kv - 1) tc_commit_warp(BAR(kBarQFree));  // the item's last QK
+        }
       }
-      // All MMAs this warp issued must retire before TMEM is released.
-      tc_commit_warp(BAR(kBarDone));
-      mbar_wait_drain(BAR(kBarDone), 0);
-      __syncwarp();
+      tA += nA;
+      tB += nB;
     }
+    // All MMAs this warp issued must retire before TMEM is released.
+    tc_commit_warp(BAR(kBarDone));
+    mbar_wait_drain(BAR(kBarDone), 0);
+    __syncwarp();
   }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(AX_SOFTMAX_REGS));
     // ------------------------------------------------------------- softmax --
     const int X = warp >> 2;              // 0: tile A, 1: tile B
     const int t = threadIdx.x & 127;      // row within the tile == TMEM lane
-    const int row = q0 + X * kTileM + t;
-    const int nX = X ? nB : nA;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + X * 128;
     const uint32_t o_addr = tmem + lane_base + kColO + X * 128;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nX; ++j) {
-      ok = mbar_wait(BAR(kBarSFull + X), static_cast<uint32_t>(j & 1), abort_flag, p.status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t s[4][32];
-      tmem_ld32(s_addr + 0, s[0]);
-      tmem_ld32(s_addr + 32, s[1]);
-      tmem_ld32(s_addr + 64, s[2]);
-      tmem_ld32(s_addr + 96, s[3]);
-      tmem_ld_wait(s[0]);
-      asm volatile("" : AX_RW32(s[1])::"memory");
-      asm volatile("" : AX_RW32(s[2])::"memory");
-      asm volatile("" : AX_RW32(s[3])::"memory");
-
-      const int key0 = j * kTileN;
-      if ((key0 + kTileN > valid) || (p.causal && key0 + kTileN - 1 > row)) {
-        const int lim = p.causal ? min(valid, row + 1) : valid;  // keys >= lim are masked
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (key0 + c >= lim) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-      }
-      // Row max: 8 independent chains of three-input max over 16 values each.
-#define SV(c) __uint_as_float(s[(c) >> 5][(c) & 31])
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        mx[i] = fmax3(SV(i), SV(i + 8), SV(i + 16));
-#pragma unroll
-        for (int c = 24; c < 120; c += 16) mx[i] = fmax3(mx[i], SV(c + i), SV(c + 8 + i));
-        mx[i] = fmaxf(mx[i], SV(120 + i));
-      }
-#undef SV
-      const float tmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
-                               fmaxf(mx[6], mx[7])) * sl2;
-      const float m_new = fmaxf(m, tmax);
-      const bool grow = m_new > m + kRescaleThreshold;  // also true on the first tile
-      const float alpha = grow ? ex2_approx(m - m_new) : 1.f;  // 0 on the first tile (m = -inf)
-      if (grow) {
-        l *= alpha;
-        m = m_new;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
-        // is stable; PV_X(j) starts only after this thread's first arrival below.
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c4 * 32, o);
-          tmem_ld_wait(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_addr + c4 * 32, o);
-        }
-      }
-      const float neg_m = (m == -INFINITY) ? 0.f : -m;
-      const float2 sl2v = make_float2(sl2, sl2);
-      const float2 nmv = make_float2(neg_m, neg_m);
-      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                       make_float2(0.f, 0.f)};
-      uint32_t pk[2][32];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int c = half * 64; c < half * 64 + 64; c += 2) {
-          const float2 x = fma2(make_float2(__uint_as_float(s[c >> 5][c & 31]),
-                                            __uint_as_float(s[c >> 5][(c + 1) & 31])),
-                                sl2v, nmv);
-          float2 pr;
-          if (((c >> 1) & 7) < kPolyPairsPer8) {
-            pr = ex2_poly2(x);
-          } else {
-            pr.x = ex2_approx(x.x);
-            pr.y = ex2_approx(x.y);
-          }
-          acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
-          pk[half][(c >> 1) & 31] = pack_half2(pr.x, pr.y);
-        }
-        // Publish this half of P: the MMA warp starts its half of PV_X(j) while
-        // the second half is still being computed.
-        tmem_st32(s_addr + half * 32, pk[half]);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(BAR(kBarPHalf + 2 * X + half));
-      }
-      const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
-      const float2 a = add2(a01, a23);
-      l += a.x + a.y;
-    }
-    if (ok && nX > 0) {
-      ok = mbar_wait(BAR(kBarODone + X), 0, abort_flag, p.status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
+    uint32_t tX = 0;  // tiles of this query tile processed in earlier items
+    uint32_t eX = 0;  // epilogues done in earlier items
+    for (int w = w0; ok && w < p.n_items; w += wstep) {
+      const Item I = item_of(w);
+      const int row = I.q0 + X * kTileM + t;
+      const int nX = X ? I.nB : I.nA;
+      const int valid = I.valid;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < nX; ++j) {
+        ok = mbar_wait(BAR(kBarSFull + X), (tX + j) & 1u, abort_flag, p.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
         tc_fence_after();
-        const float inv_l = 1.f / l;
-        __half* orow = p.o + static_cast<long long>(b) * p.o_batch +
-                       static_cast<long long>(row) * p.o_tok +
-                       static_cast<long long>(h - p.o_head_base) * p.o_head;
+        uint32_t s[4][32];
+        tmem_ld32(s_addr + 0, s[0]);
+        tmem_ld32(s_addr + 32, s[1]);
+        tmem_ld32(s_addr + 64, s[2]);
+        tmem_ld32(s_addr + 96, s[3]);
+        tmem_ld_wait(s[0]);
+        asm volatile("" : AX_RW32(s[1])::"memory");
+        asm volatile("" : AX_RW32(s[2])::"memory");
+        asm volatile("" : AX_RW32(s[3])::"memory");
+
+        const int key0 = j * kTileN;
+        if ((key0 + kTileN > valid) || (p.causal && key0 + kTileN - 1 > row)) {
+          const int lim = p.causal ? min(valid, row + 1) : valid;  // keys >= lim are masked
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c4 * 32, o);
-          tmem_ld_wait(o);
-          if (row < p.q_len) {
+          for (int c = 0; c < 128; ++c)
+            if (key0 + c >= lim) s[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+        }
+        // Row max: 8 independent chains of three-input max over 16 values each.
+#define SV(c) __uint_as_float(s[(c) >> 5][(c) & 31])
+        float mx[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l);
-              v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
-              v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
-              v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + c4 * 32 + i * 8) = v;
+        for (int i = 0; i < 8; ++i) {
+          mx[i] = fmax3(SV(i), SV(i + 8), SV(i + 16));
+#pragma unroll
+          for (int c = 24; c < 120; c += 16) mx[i] = fmax3(mx[i], SV(c + i), SV(c + 8 + i));
+          mx[i] = fmaxf(mx[i], SV(120 + i));
+        }
+#undef SV
+        const float tmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                                 fmaxf(mx[6], mx[7])) * sl2;
+        const float m_new = fmaxf(m, tmax);
+        const bool grow = m_new > m + kRescaleThreshold;  // also true on the first tile
+        const float alpha = grow ? ex2_approx(m - m_new) : 1.f;  // 0 on the first tile (m = -inf)
+        if (grow) {
+          l *= alpha;
+          m = m_new;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
+          // is stable; PV_X(j) starts only after this thread's first arrival below.
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c4 * 32, o);
+            tmem_ld_wait(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_addr + c4 * 32, o);
+          }
+        }
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        const float2 sl2v = make_float2(sl2, sl2);
+        const float2 nmv = make_float2(neg_m, neg_m);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+        uint32_t pk[2][32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int c = half * 64; c < half * 64 + 64; c += 2) {
+            const float2 x = fma2(make_float2(__uint_as_float(s[c >> 5][c & 31]),
+                                              __uint_as_float(s[c >> 5][(c + 1) & 31])),
+                                  sl2v, nmv);
+            float2 pr;
+            if (((c >> 1) & 7) < kPolyPairsPer8) {
+              pr = ex2_poly2(x);
+            } else {
+              pr.x = ex2_approx(x.x);
+              pr.y = ex2_approx(x.y);
+            }
+            acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
+            pk[half][(c >> 1) & 31] = pack_half2(pr.x, pr.y);
+          }
+          // Publish this half of P: the MMA warp starts its half of PV_X(j) while
+          // the second half is still being computed.
+          tmem_st32(s_addr + half * 32, pk[half]);
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(BAR(kBarPHalf + 2 * X + half));
+        }
+        const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+        const float2 a = add2(a01, a23);
+        l += a.x + a.y;
+      }
+      if (ok && nX > 0) {
+        ok = mbar_wait(BAR(kBarODone + X), eX & 1u, abort_flag, p.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          const float inv_l = 1.f / l;
+          __half* orow = p.o + static_cast<long long>(I.b) * p.o_batch +
+                         static_cast<long long>(row) * p.o_tok +
+                         static_cast<long long>(I.h - p.o_head_base) * p.o_head;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c4 * 32, o);
+            tmem_ld_wait(o);
+            if (row < p.q_len) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                uint4 v;
+                v.x = pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l);
+                v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
+                v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
+                v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
+                *reinterpret_cast<uint4*>(orow + c4 * 32 + i * 8) = v;
+              }
             }
           }
         }
+        ++eX;
       }
+      tX += nX;
     }
   }
 
@@ -478,8 +537,22 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  dim3 grid(p.n_q_tiles, heads_in_launch, batch);
-  attn_fwd_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+  // Persistent grid: one CTA per SM (at most one per work item).
+  static std::atomic<int> sm_count[64];
+  int sms = sm_count[dev & 63].load(std::memory_order_relaxed);
+  if (sms == 0) {
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sm_count[dev & 63].store(sms, std::memory_order_relaxed);
+  }
+  AttnFwdParams q = p;
+  q.heads_in_launch = heads_in_launch;
+  const long long items = static_cast<long long>(p.n_q_tiles) * heads_in_launch * batch;
+  if (items <= 0) return cudaSuccess;
+  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  q.n_items = static_cast<int>(items);
+  const int grid = static_cast<int>(items < sms ? items : sms);
+  attn_fwd_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, q);
   return cudaGetLastError();
 }
 

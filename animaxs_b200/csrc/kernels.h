@@ -18,8 +18,10 @@ struct AttnFwdParams {
   int kv_valid;          // keys >= kv_valid masked (already clamped to [1, kv_len])
   const int* kv_valid_dev;  // optional per-batch override (device)
   int causal;
-  int n_q_tiles;         // CTAs along the query axis: ceil(q_len / attn_fwd_rows_per_cta())
+  int n_q_tiles;         // query-tile pairs per head: ceil(q_len / attn_fwd_rows_per_cta())
   int head_offset;       // first query head handled by this launch
+  int heads_in_launch;   // set by launch_attn_fwd: query heads of this launch
+  int n_items;           // set by launch_attn_fwd: n_q_tiles * heads_in_launch * batch
   int o_head_base;       // output head index = h - o_head_base
   float scale_log2;      // softmax scale * log2(e)
   __half* o;
