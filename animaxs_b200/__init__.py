@@ -9,4 +9,4 @@ package holds its CUDA sources (``csrc/``), the in-tree build
 from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError,  # noqa: F401
                    AttentionValidationError, LIB_PATH, lib)
 from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  # noqa: F401
-                       DitRoPE, GqaHeadMapping, qwen_rope)
+                       DitRoPE, GqaHeadMapping, adapter_rope, qwen_rope)

@@ -56,14 +56,15 @@ def check_register_split(source: str, ptxas_log: str) -> None:
     threads = int(re.search(r"constexpr int kThreads = (\d+);", text).group(1))
     ms = re.search(r"constexpr int kSoftmaxThreads = (\d+);", text)
     softmax_threads = int(ms.group(1)) if ms else 256
-    m = re.search(r"attn_fwd_sm100_kernel.*?Used (\d+) registers", ptxas_log, re.S)
-    if m is None:
+    counts = re.findall(r"entry function '[^']*attn_fwd_sm100_kernel[^']*'.*?Used (\d+) registers",
+                        ptxas_log, re.S)
+    if not counts:
         raise RuntimeError("could not read the flash kernel's register count from ptxas")
-    launch = int(m.group(1))
     need = softmax_threads * soft + (threads - softmax_threads) * other
-    if need > threads * launch or soft % 8 or other % 8:
-        raise RuntimeError(f"register split {softmax_threads}x{soft} + {threads - softmax_threads}x{other} "
-                           f"= {need} exceeds the launch allocation {threads}x{launch} = {threads * launch}")
+    for launch in map(int, counts):  # one per head-dim instantiation
+        if need > threads * launch or soft % 8 or other % 8:
+            raise RuntimeError(f"register split {softmax_threads}x{soft} + {threads - softmax_threads}x{other} "
+                               f"= {need} exceeds the launch allocation {threads}x{launch} = {threads * launch}")
 
 
 def build(force: bool = False, verbose: bool = False) -> str:

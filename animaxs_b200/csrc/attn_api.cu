@@ -168,9 +168,9 @@ int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q
   if (d->batch <= 0 || d->heads <= 0 || d->q_len <= 0 || d->kv_len <= 0 || d->head_dim <= 0 ||
       d->kv_heads <= 0 || d->heads % d->kv_heads != 0 || (d->causal && d->q_len != d->kv_len))
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "%s", kShapeMsg);
-  if (d->head_dim != ax::kHeadDim)
+  if (d->head_dim != 128 && d->head_dim != 64)
     return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
-                        "attention on B200 requires headDim == 128 (got %d)", d->head_dim);
+                        "attention on B200 requires headDim 128 or 64 (got %d)", d->head_dim);
   if (d->kv_valid_len < 0 || d->kv_valid_len > d->kv_len)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
                         "kv_valid_len %d outside [0, keyCount %d]", d->kv_valid_len, d->kv_len);
@@ -254,16 +254,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [batch][heads][rows][128] fp16 view; box = 64 columns x 128 rows, 128B swizzle.
-int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int64_t rows,
+// [batch][heads][rows][dim] fp16 view (dim 64 or 128); box = 64 columns x 128
+// rows, 128B swizzle.
+int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int64_t dim, int64_t rows,
                  int64_t heads, int64_t batch, int64_t st, int64_t sh, int64_t sb) {
   auto fn = encode_fn();
   if (fn == nullptr)
     return ax_set_error(ctx, ANIMAXS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   // A stride of a dimension of extent 1 is never used for addressing but must
   // still satisfy the encoder's rules; substitute a legal value.
-  const int64_t fallback = 128 * 2;
-  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(heads),
+  const int64_t fallback = dim * 2;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(heads),
                         static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(rows > 1 ? st * 2 : fallback),
                            static_cast<cuuint64_t>(heads > 1 ? sh * 2 : fallback),
@@ -324,6 +325,7 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     __half* kn = reinterpret_cast<__half*>(static_cast<char*>(ctx->scratch) +
                                            ((q_bytes + 255) & ~static_cast<int64_t>(255)));
     NormParams np{};
+    np.head_dim = static_cast<int>(d->head_dim);
     np.eps = d->eps > 0.f ? d->eps : 1e-6f;
     np.rope = d->qk_norm == ANIMAXS_QK_RMS_ROPE ? d->rope_table : nullptr;
     // Only the query heads this call computes need normalising.
@@ -373,15 +375,16 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   }
 
   CUtensorMap tq, tk, tv;
-  int rc = ax_make_tmap(ctx, &tq, qa, d->q_len, d->heads, d->batch, q_st, q_sh, q_sb);
+  int rc = ax_make_tmap(ctx, &tq, qa, d->head_dim, d->q_len, d->heads, d->batch, q_st, q_sh, q_sb);
   if (rc == ANIMAXS_OK)
-    rc = ax_make_tmap(ctx, &tk, ka, d->kv_len, d->kv_heads, d->batch, k_st, k_sh, k_sb);
+    rc = ax_make_tmap(ctx, &tk, ka, d->head_dim, d->kv_len, d->kv_heads, d->batch, k_st, k_sh, k_sb);
   if (rc == ANIMAXS_OK)
-    rc = ax_make_tmap(ctx, &tv, v, d->kv_len, d->kv_heads, d->batch, d->v_tok_stride,
+    rc = ax_make_tmap(ctx, &tv, v, d->head_dim, d->kv_len, d->kv_heads, d->batch, d->v_tok_stride,
                       d->v_head_stride, d->v_batch_stride);
   if (rc != ANIMAXS_OK) return rc;
 
   AttnFwdParams p{};
+  p.head_dim = static_cast<int>(d->head_dim);
   p.q_len = d->q_len;
   p.kv_len = d->kv_len;
   p.heads_per_kv = d->heads / d->kv_heads;
@@ -500,8 +503,8 @@ static int norm_standalone(animaxs_attn_ctx* ctx, const void* in, void* out, con
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "null buffer");
   if (tokens <= 0 || heads <= 0)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "invalid rms norm shape");
-  if (head_dim != ax::kHeadDim)
-    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED, "rms norm requires headDim == 128");
+  if (head_dim != 128 && head_dim != 64)
+    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED, "rms norm requires headDim 128 or 64");
   if (row_stride == 0) row_stride = static_cast<int64_t>(heads) * head_dim;
   if (row_stride < static_cast<int64_t>(heads) * head_dim || row_stride % 8 != 0 ||
       reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
@@ -510,6 +513,7 @@ static int norm_standalone(animaxs_attn_ctx* ctx, const void* in, void* out, con
                         "rms norm requires 16-byte-aligned buffers and row stride");
   if (!(eps >= 0.f)) return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "eps must be >= 0");
   NormParams np{};
+  np.head_dim = head_dim;
   np.eps = eps > 0.f ? eps : 1e-6f;
   np.rope = rope;
   NormJob& j = np.job[0];

@@ -47,18 +47,23 @@
 namespace ax {
 namespace {
 
-constexpr uint32_t kTileBytes = kTileM * kHeadDim * 2;  // 32 KiB: one 128x128 fp16 tile
 constexpr uint32_t kPanelBytes = 128 * 128;             // 128 rows x 128 B (64 fp16)
-constexpr uint32_t kSmQ = 0;                            // Q_A, Q_B
 // Ring depths.  A tile load measured ~4000 cycles from issue to arrival under
 // full load; two stages each cover it (a third V stage, which still fits in
 // 227 KiB, measured no faster).
 constexpr int kKStages = 2;
 constexpr int kVStages = 2;
-constexpr uint32_t kSmK = kSmQ + 2 * kTileBytes;
-constexpr uint32_t kSmV = kSmK + kKStages * kTileBytes;
-constexpr uint32_t kSmBar = kSmV + kVStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kSmBar + 256 + 1024;    // + barriers + alignment slack
+// Shared-memory layout for head dim HD (64 or 128): a Q/K/V tile is 128 rows x HD
+// fp16 = HD/64 swizzled 64-column panels.
+template <int HD>
+struct Smem {
+  static constexpr uint32_t kTile = kTileM * HD * 2;     // 32 KiB (HD 128) / 16 KiB (HD 64)
+  static constexpr uint32_t kQ = 0;                      // Q_A, Q_B
+  static constexpr uint32_t kK = kQ + 2 * kTile;
+  static constexpr uint32_t kV = kK + kKStages * kTile;
+  static constexpr uint32_t kBar = kV + kVStages * kTile;
+  static constexpr uint32_t kBytes = kBar + 256 + 1024;  // + barriers + alignment slack
+};
 constexpr int kThreads = 384;  // warpgroups: softmax A, softmax B, MMA/TMA (+2 idle warps)
 
 enum : int {
@@ -75,14 +80,15 @@ enum : int {
   kNumBars = kBarDone + 1
 };
 static_assert(kNumBars * 8 + 8 <= 256, "barrier block overflows its 256 bytes");
-static_assert(kSmBar + 256 + 1024 <= 227 * 1024, "shared memory exceeds the 227 KiB opt-in");
+static_assert(Smem<128>::kBytes <= 227 * 1024, "shared memory exceeds the 227 KiB opt-in");
 constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;
+constexpr uint32_t kColO = 256;  // O_A at kColO, O_B at kColO + HD
 constexpr uint32_t kIdescQK = idesc_f16_f32(128, 128, false);  // B = K tile, K-major
-constexpr uint32_t kIdescPV = idesc_f16_f32(128, 128, true);   // B = V tile, MN-major
+template <int HD>
+constexpr uint32_t kIdescPV = idesc_f16_f32(128, HD, true);     // B = V tile, MN-major, N = HD
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled when max grows > 2^8
 // Of every 8 adjacent column pairs, this many take exp2 on the FMA pipe
 // (polynomial) and the rest on the MUFU pipe.
@@ -137,22 +143,24 @@ __device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile, int kk) {
 // (bits 0-13, address >> 4; every operand lies below 256 KiB of shared memory,
 // so the field never carries).  The loops are unrolled and run on the whole MMA
 // warp (one elected lane issues): the issue rate sits on the critical path.
+template <int HD>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint32_t k_tile) {
   const uint64_t a0 = kmajor_desc(q_tile, 0), b0 = kmajor_desc(k_tile, 0);
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
+  for (int kk = 0; kk < HD / 16; ++kk) {
     const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4);
     umma_f16_ss_warp(d_tmem, a0 + off, b0 + off, kIdescQK, kk > 0 ? 1u : 0u);
   }
 }
 // Half `hf` of O (+)= P V: k-steps 4*hf .. 4*hf+3 (keys [64*hf, 64*hf+64)).
+template <int HD>
 __device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
                                               int hf, bool accumulate) {
   const uint64_t b0 = vmajor_desc(v_tile, 0);
 #pragma unroll
   for (int k4 = 0; k4 < 4; ++k4) {
     const int kk = hf * 4 + k4;
-    umma_f16_ts_warp(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
+    umma_f16_ts_warp(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV<HD>,
                 (accumulate || kk > 0) ? 1u : 0u);
   }
 }
@@ -164,6 +172,7 @@ __device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, i
   return (e + kTileN - 1) / kTileN;
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -172,10 +181,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t sQ = base + kSmQ, sK = base + kSmK, sV = base + kSmV;
-  const uint32_t bar0 = base + kSmBar;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + kSmBar + kSlotTmem);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kSmBar + kSlotAbort);
+  using L = Smem<HD>;
+  constexpr uint32_t kTileBytes = L::kTile;
+  const uint32_t sQ = base + L::kQ, sK = base + L::kK, sV = base + L::kV;
+  const uint32_t bar0 = base + L::kBar;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kBar + kSlotTmem);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kBar + kSlotAbort);
 #define BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
 
   const int warp = threadIdx.x >> 5;
@@ -244,8 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(BAR((is_k ? kBarKEmpty : kBarVEmpty) + st), ph ^ 1u, abort_flag, p.status))
           return false;
         mbar_arrive_expect_tx(full, kTileBytes);
-        tma_load_4d(dst, tm, full, 0, row0, kvh, b);
-        tma_load_4d(dst + kPanelBytes, tm, full, 64, row0, kvh, b);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) tma_load_4d(dst + c * kPanelBytes, tm, full, 64 * c, row0, kvh, b);
         ++(is_k ? armed_k[st] : armed_v[st]);
         return true;
       };
@@ -258,10 +269,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        abort_flag, p.status)))
           break;
         mbar_arrive_expect_tx(BAR(kBarQ), 2 * kTileBytes);
-        tma_load_4d(sQ, &tm_q, BAR(kBarQ), 0, I.q0, I.h, I.b);
-        tma_load_4d(sQ + kPanelBytes, &tm_q, BAR(kBarQ), 64, I.q0, I.h, I.b);
-        tma_load_4d(sQ + kTileBytes, &tm_q, BAR(kBarQ), 0, I.q0 + kTileM, I.h, I.b);
-        tma_load_4d(sQ + kTileBytes + kPanelBytes, &tm_q, BAR(kBarQ), 64, I.q0 + kTileM, I.h, I.b);
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_4d(sQ + x * kTileBytes + c * kPanelBytes, &tm_q, BAR(kBarQ), 64 * c,
+                        I.q0 + x * kTileM, I.h, I.b);
         ++armed_q;
         // K/V in the order the MMA warp consumes them: K_0, then V_j, K_{j+1}.
         if (!(ok = load(true, gk++, 0, I.kvh, I.b))) break;
@@ -299,11 +312,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t k0 = sK + (gk % kKStages) * kTileBytes;
       if (nA > 0) {
-        issue_qk(tmem + 0, sQA, k0);
+        issue_qk<HD>(tmem + 0, sQA, k0);
         tc_commit_warp(BAR(kBarSFull + 0));
       }
       if (nB > 0) {
-        issue_qk(tmem + 128, sQB, k0);
+        issue_qk<HD>(tmem + 128, sQB, k0);
         tc_commit_warp(BAR(kBarSFull + 1));
       }
       tc_commit_warp(BAR(kBarKEmpty + gk % kKStages));
@@ -323,10 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t pph = (tA + j) & 1u;
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 0), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half(tmem + kColO, tmem + 0, vt, 0, j > 0);
+          issue_pv_half<HD>(tmem + kColO, tmem + 0, vt, 0, j > 0);
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 1), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half(tmem + kColO, tmem + 0, vt, 1, true);
+          issue_pv_half<HD>(tmem + kColO, tmem + 0, vt, 1, true);
           if (j == nA - 1) tc_commit_warp(BAR(kBarODone + 0));
         }
         if (j1 < n_kv) {
@@ -334,17 +347,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         if (j1 < nA) {
-          issue_qk(tmem + 0, sQA, kt1);
+          issue_qk<HD>(tmem + 0, sQA, kt1);
           tc_commit_warp(BAR(kBarSFull + 0));
         }
         if (j < nB) {
           const uint32_t pph = (tB + j) & 1u;
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 2), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half(tmem + kColO + 128, tmem + 128, vt, 0, j > 0);
+          issue_pv_half<HD>(tmem + kColO + HD, tmem + 128, vt, 0, j > 0);
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 3), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half(tmem + kColO + 128, tmem + 128, vt, 1, true);
+          issue_pv_half<HD>(tmem + kColO + HD, tmem + 128, vt, 1, true);
           if (j == nB - 1) tc_commit_warp(BAR(kBarODone + 1));
         }
         // V_j's last reader has been issued: release its stage now (the commit
@@ -352,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit_warp(BAR(kBarVEmpty + vst));
         ++gv;
         if (j1 < nB) {
-          issue_qk(tmem + 128, sQB, kt1);
+          issue_qk<HD>(tmem + 128, sQB, kt1);
           tc_commit_warp(BAR(kBarSFull + 1));
         }
         if (j1 < n_kv) {
@@ -376,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x & 127;      // row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + X * 128;
-    const uint32_t o_addr = tmem + lane_base + kColO + X * 128;
+    const uint32_t o_addr = tmem + lane_base + kColO + X * HD;
     const float sl2 = p.scale_log2;
     bool ok = true;
     uint32_t tX = 0;  // tiles of this query tile processed in earlier items
@@ -433,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // PV_X(j-1) precedes QK_X(j) in the MMA stream, so it has retired and O
           // is stable; PV_X(j) starts only after this thread's first arrival below.
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
+          for (int c4 = 0; c4 < HD / 32; ++c4) {
             uint32_t o[32];
             tmem_ld32(o_addr + c4 * 32, o);
             tmem_ld_wait(o);
@@ -486,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          static_cast<long long>(row) * p.o_tok +
                          static_cast<long long>(I.h - p.o_head_base) * p.o_head;
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
+          for (int c4 = 0; c4 < HD / 32; ++c4) {
             uint32_t o[32];
             tmem_ld32(o_addr + c4 * 32, o);
             tmem_ld_wait(o);
@@ -522,18 +535,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int attn_fwd_rows_per_cta() { return 2 * kTileM; }
 
-cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                            const AttnFwdParams& p, int heads_in_launch, int batch,
-                            cudaStream_t stream) {
+template <int HD>
+static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const AttnFwdParams& p, int heads_in_launch, int batch, int dev,
+                             cudaStream_t stream) {
   // The dynamic shared-memory opt-in is a per-device function attribute.
   static std::atomic<uint64_t> configured{0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
+  cudaError_t e;
   const uint64_t bit = 1ull << (dev & 63);
   if ((configured.load(std::memory_order_acquire) & bit) == 0) {
-    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes);
+    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Smem<HD>::kBytes);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -552,8 +564,19 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   q.n_items = static_cast<int>(items);
   const int grid = static_cast<int>(items < sms ? items : sms);
-  attn_fwd_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, q);
+  attn_fwd_sm100_kernel<HD><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, q);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                            const AttnFwdParams& p, int heads_in_launch, int batch,
+                            cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (p.head_dim == 64) return launch_hd<64>(tq, tk, tv, p, heads_in_launch, batch, dev, stream);
+  if (p.head_dim == 128) return launch_hd<128>(tq, tk, tv, p, heads_in_launch, batch, dev, stream);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace ax

@@ -9,9 +9,10 @@
 namespace ax {
 
 // Parameters of the flash-attention kernel (attn_fwd_sm100.cu).  q/k/v arrive
-// through TMA tensor maps over [batch][head][token][128] fp16 views (any
+// through TMA tensor maps over [batch][head][token][head_dim] fp16 views (any
 // strides); the output is written with plain stores.
 struct AttnFwdParams {
+  int head_dim;          // 64 or 128
   int q_len;
   int kv_len;
   int heads_per_kv;      // heads / kv_heads (GQA group size)
@@ -33,9 +34,9 @@ constexpr unsigned int kStatusTimeoutBit = 1u;  // a bounded device wait expired
 
 constexpr int kTileM = 128;   // query rows per CTA
 constexpr int kTileN = 128;   // keys per K/V tile
-constexpr int kHeadDim = 128;
+constexpr int kHeadDim = 128;   // DiT / Qwen; the LLM adapter runs 64
 
-// One normalisation job: a [batch][tokens][heads][128] fp16 tensor with strides.
+// One normalisation job: a [batch][tokens][heads][head_dim] fp16 tensor with strides.
 struct NormJob {
   const __half* in;
   __half* out;
@@ -49,8 +50,9 @@ struct NormJob {
 struct NormParams {
   NormJob job[2];
   int njobs;
+  int head_dim;          // 64 or 128
   float eps;
-  const float* rope;     // [tokens][64][2][2] or nullptr (no rotation)
+  const float* rope;     // [tokens][head_dim/2][2][2] or nullptr (no rotation)
   unsigned int* status;  // device status word (nullable)
 
 };

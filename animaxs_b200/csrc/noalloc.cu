@@ -95,6 +95,7 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
     __half* kn = reinterpret_cast<__half*>(static_cast<char*>(scratch) +
                                            ((q_bytes + 255) & ~static_cast<int64_t>(255)));
     ax::NormParams np{};
+    np.head_dim = static_cast<int>(d->head_dim);
     np.eps = d->eps > 0.f ? d->eps : 1e-6f;
     np.rope = d->qk_norm == ANIMAXS_QK_RMS_ROPE ? d->rope_table : nullptr;
     ax::NormJob& jq = np.job[0];
@@ -138,15 +139,16 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
   }
 
   CUtensorMap tq, tk, tv;
-  rc = ax_make_tmap(nullptr, &tq, qa, d->q_len, d->heads, d->batch, q_st, q_sh, q_sb);
+  rc = ax_make_tmap(nullptr, &tq, qa, d->head_dim, d->q_len, d->heads, d->batch, q_st, q_sh, q_sb);
   if (rc == ANIMAXS_OK)
-    rc = ax_make_tmap(nullptr, &tk, ka, d->kv_len, d->kv_heads, d->batch, k_st, k_sh, k_sb);
+    rc = ax_make_tmap(nullptr, &tk, ka, d->head_dim, d->kv_len, d->kv_heads, d->batch, k_st, k_sh, k_sb);
   if (rc == ANIMAXS_OK)
-    rc = ax_make_tmap(nullptr, &tv, v, d->kv_len, d->kv_heads, d->batch, d->v_tok_stride,
+    rc = ax_make_tmap(nullptr, &tv, v, d->head_dim, d->kv_len, d->kv_heads, d->batch, d->v_tok_stride,
                       d->v_head_stride, d->v_batch_stride);
   if (rc != ANIMAXS_OK) return rc;
 
   ax::AttnFwdParams p{};
+  p.head_dim = static_cast<int>(d->head_dim);
   p.q_len = d->q_len;
   p.kv_len = d->kv_len;
   p.heads_per_kv = d->heads / d->kv_heads;

@@ -82,14 +82,15 @@ ncclResult_t settle(NcclApi* api, ncclComm_t comm, double seconds) {
   }
 }
 
-// gather[r][b][s][hl][128] -> o[b*ob + s*ot + (r*hr + hl)*oh], 16 B per thread.
+// gather[r][b][s][hl][D] -> o[b*ob + s*ot + (r*hr + hl)*oh], 16 B per thread;
+// a head row is D/8 = 1 << chunk_shift chunks of 16 B.
 __global__ void permute_heads_kernel(const uint4* __restrict__ gather, __half* __restrict__ o,
                                      long long total16, int world, int batch, int q_len, int hr,
-                                     long long ot, long long oh, long long ob) {
+                                     long long ot, long long oh, long long ob, int chunk_shift) {
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total16) return;
-  const int c16 = static_cast<int>(i & 15);
-  long long r = i >> 4;
+  const int c16 = static_cast<int>(i & ((1 << chunk_shift) - 1));
+  long long r = i >> chunk_shift;
   const int hl = static_cast<int>(r % hr);
   r /= hr;
   const int s = static_cast<int>(r % q_len);
@@ -244,7 +245,8 @@ extern "C" int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_
     permute_heads_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(gather),
                                                      static_cast<__half*>(o), total16, world,
                                                      d->batch, d->q_len, hr, d->o_tok_stride,
-                                                     d->o_head_stride, d->o_batch_stride);
+                                                     d->o_head_stride, d->o_batch_stride,
+                                                     D == 64 ? 3 : 4);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       cudaSetDevice(prev);

@@ -238,7 +238,7 @@ class AttentionExecutor:
     def strided_desc(self, q, k, v, out, *, causal=False, qk_norm="none", rope_table=None,
                      q_norm_weight=None, k_norm_weight=None, eps=1e-6, kv_valid_len=None,
                      kv_valid_lens=None, scale=None) -> AttnDesc:
-        """Descriptor for ``[B, S, H, 128]`` tensors with arbitrary strides (cached)."""
+        """Descriptor for ``[B, S, H, D]`` tensors (D 128 or 64) with arbitrary strides (cached)."""
         key = (q.shape, k.shape, q.stride(), k.stride(), v.stride(), out.stride(), causal, qk_norm,
                None if rope_table is None else (rope_table.data_ptr(), rope_table.numel()),
                None if q_norm_weight is None else q_norm_weight.data_ptr(),
@@ -267,8 +267,8 @@ class AttentionExecutor:
         return desc
 
     def attention(self, q, k, v, out=None, *, stream=None, **kw):
-        """Strided entry: ``q``/``out`` are ``[B, Sq, H, 128]`` and ``k``/``v``
-        ``[B, Sk, Hkv, 128]`` fp16 device tensors with ANY strides (token-major,
+        """Strided entry: ``q``/``out`` are ``[B, Sq, H, D]`` and ``k``/``v``
+        ``[B, Sk, Hkv, D]`` fp16 device tensors, D 128 or 64, with ANY strides (token-major,
         head-major views, batch gaps).  Keywords: ``causal``, ``qk_norm``
         (``"none"``/``"rms"``/``"rms_rope"``), ``rope_table``, ``q_norm_weight``,
         ``k_norm_weight``, ``eps``, ``kv_valid_len``, ``kv_valid_lens``, ``scale``.
@@ -332,6 +332,13 @@ def qwen_rope(tokens: int, theta: float = 1.0e6, head_dim: int = 128) -> np.ndar
                                     out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
     raise_for(rc, "invalid rope length")
     return out
+
+
+def adapter_rope(tokens: int) -> np.ndarray:
+    """LLMAdapterMetal.makeRope(tokens:) (LLMAdapterMetal.swift:162-178): the
+    LLM adapter's [tokens][32][2][2] table (theta 1e4, 64-wide heads) for
+    ``qk_norm="rms_rope"`` on head_dim-64 calls."""
+    return qwen_rope(tokens, theta=1.0e4, head_dim=64)
 
 
 class GqaHeadMapping:

@@ -84,7 +84,8 @@ typedef struct animaxs_attn_desc {
   int32_t kv_heads;     /* `keyValueHeads:`; query head h reads kv head h / (heads/kv_heads) */
   int32_t q_len;        /* `queryCount:` */
   int32_t kv_len;       /* `keyCount:` */
-  int32_t head_dim;     /* `headDim:`; this build runs 128 */
+  int32_t head_dim;     /* `headDim:`; this build runs 128 (DiT, Qwen) and 64 (LLM adapter,
+                           LLMAdapterMetal.swift:9-10,394-397); others -> UNSUPPORTED */
   int64_t q_tok_stride, q_head_stride, q_batch_stride;
   int64_t k_tok_stride, k_head_stride, k_batch_stride;
   int64_t v_tok_stride, v_head_stride, v_batch_stride;
@@ -173,7 +174,8 @@ int animaxs_attn_kernel_timing(animaxs_attn_ctx* ctx, int64_t* launches, double*
 /* Standalone per-(token, head) RMSNorm + split-half RoPE, fp16 in/out
  * ([tokens, heads, head_dim] rows, `row_stride` elements apart per token),
  * in place allowed.  Replaces kernel rms_rope_split_half
- * (AnimaKernels.metal:696-729).  `rope_table` is DEVICE fp32
+ * (AnimaKernels.metal:696-729) at head_dim 128 and rms_rope_adapter64
+ * (AnimaKernels.metal:733-763) at head_dim 64.  `rope_table` is DEVICE fp32
  * [tokens][head_dim/2][2][2]; `weight` DEVICE fp16[head_dim] or NULL. */
 int animaxs_rms_rope_split_half(animaxs_attn_ctx* ctx, const void* in, void* out,
                                 const void* weight, const float* rope_table,
@@ -194,7 +196,9 @@ int animaxs_rope3d_table(int T, int H, int W, float* out);
 
 /* 1-D NeoX RoPE table [seq_len][head_dim/2][2][2] fp32, inv_freq =
  * theta^(-2p/head_dim).  Replaces QwenEncoderMetal.makeRope(tokens:)
- * (QwenEncoderMetal.swift:126-142, theta 1e6). */
+ * (QwenEncoderMetal.swift:126-142: head_dim 128, theta 1e6) and
+ * LLMAdapterMetal.makeRope(tokens:key:) (LLMAdapterMetal.swift:162-178:
+ * head_dim 64, theta 1e4). */
 int animaxs_rope1d_table(int seq_len, int head_dim, double theta, float* out);
 
 /* GQA head map: kv head read by query head `query_head`

@@ -144,6 +144,23 @@ def rope1d_table(seq_len: int, theta: float = 1.0e6, head_dim: int = HEAD_DIM) -
     return np.ascontiguousarray(_blocks(np.outer(pos, inv)).reshape(seq_len, head_dim // 2, 2, 2))
 
 
+# LLM adapter attention heads are 64 wide (LLMAdapterMetal.swift:9-10).
+ADAPTER_HEAD_DIM = 64
+
+
+def adapter_rope_table(tokens: int) -> np.ndarray:
+    """The LLM adapter's RoPE table, LLMAdapterMetal.swift:162-178 (makeRope).
+
+    32 pairs per token: ``inverse = 1 / pow(10000, 2p / 64)`` and
+    ``angle = token * inverse`` in fp32, blocks ``[cos, -sin, sin, cos]``;
+    consumed by rms_rope_adapter64 (AnimaKernels.metal:733-763), which rotates
+    the pairs ``(p, p + 32)`` exactly as ``apply_split_half_rope`` does for a
+    64-wide head.  Same construction as the 1-D table with theta 1e4 and
+    head_dim 64.
+    """
+    return rope1d_table(tokens, theta=1.0e4, head_dim=ADAPTER_HEAD_DIM)
+
+
 # ---------------------------------------------------------------------------
 # GQA and attention
 # ---------------------------------------------------------------------------

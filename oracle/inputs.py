@@ -5,7 +5,8 @@ TEST INFRASTRUCTURE ONLY (used by ``tests/``, ``smoke()`` and the CPU legs of
 this container, the GPU box and the golden-fixture script all see identical
 values: ``g = torch.Generator().manual_seed(seed)``; ``q, k, v = randn(...)``
 in that order as fp32, then rounded to fp16.  Shapes are token-major
-``[B, S, H, 128]`` -- the layout the reference's projections produce
+``[B, S, H, D]`` (D = 128; 64 for the LLM adapter) -- the layout the
+reference's projections produce
 (``DiTBlockExecutor.swift:1097-1131``, ``QwenEncoderMetal.swift:245-262``).
 """
 
@@ -98,6 +99,21 @@ def qwen_prefill(layer: int = 0, seq_len: int = 512, heads: int = 16, kv_heads: 
     return Case(f"qwen_l{layer}", q, k, v, qk_norm="rms_rope",
                 rope_table=ora.rope1d_table(seq_len, 1.0e6), causal=True,
                 kv_valid_len=None if valid is None else [valid], meta={"layer": layer})
+
+
+def adapter_attention(seed: int = 0, target_tokens: int = 512, context_tokens: int | None = None,
+                      heads: int = 16, batch: int = 1) -> Case:
+    """LLM adapter attention (LLMAdapterMetal.swift:361-404): 16 heads of 64,
+    q and k through rms_rope_adapter64 (RMSNorm, unit weights here, then the
+    adapter's RoPE), non-causal.  Self-attention over the target tokens, or
+    cross-attention from them to ``context_tokens`` rows (the Qwen context);
+    both at most 512 tokens (LLMAdapterMetal.swift:7,45-46)."""
+    kv = target_tokens if context_tokens is None else context_tokens
+    q, k, v = draw_qkv(seed, (batch, target_tokens, heads, ora.ADAPTER_HEAD_DIM),
+                       (batch, kv, heads, ora.ADAPTER_HEAD_DIM))
+    name = f"adapter_{target_tokens}x{kv}"
+    return Case(name, q, k, v, qk_norm="rms_rope",
+                rope_table=ora.adapter_rope_table(max(target_tokens, kv)))
 
 
 def workload_seed(prompt: int, step: int, block: int) -> int:

@@ -80,8 +80,10 @@ def test_validation_mirrors_reference(lib):
     assert _validate(lib, _desc(lib, q_len=0)) == -1
     assert _validate(lib, _desc(lib, causal=1, q_len=100, kv_len=200)) == -1
     assert _validate(lib, _desc(lib, causal=1, q_len=100, kv_len=100)) == 0
-    # unsupported head dim
-    assert _validate(lib, _desc(lib, head_dim=64)) == -2
+    # head dims: 128 (DiT, Qwen) and 64 (LLM adapter) run; others are unsupported
+    assert _validate(lib, _desc(lib, head_dim=64)) == 0
+    assert _validate(lib, _desc(lib, head_dim=96)) == -2
+    assert _validate(lib, _desc(lib, head_dim=32)) == -2
     # null and misaligned buffers, misaligned stride
     assert _validate(lib, ok, (0, 0x2000, 0x3000, 0x4000)) == -1
     assert _validate(lib, ok, (0x1008, 0x2000, 0x3000, 0x4000)) == -1
@@ -122,6 +124,19 @@ def test_rope1d_table_helper():
     from animaxs_b200 import qwen_rope
     got = qwen_rope(512).reshape(512, 64, 2, 2)
     np.testing.assert_allclose(got, ora.rope1d_table(512, 1e6), atol=4e-5)
+
+
+def test_adapter_rope_table_helper():
+    """LLMAdapterMetal.makeRope (LLMAdapterMetal.swift:162-178) through the C
+    helper: [tokens][32][2][2], theta 1e4, 64-wide heads."""
+    from animaxs_b200 import adapter_rope
+    got = adapter_rope(512).reshape(512, 32, 2, 2)
+    ref = ora.adapter_rope_table(512)
+    np.testing.assert_allclose(got, ref, atol=4e-5)
+    # token 1, pair 0: angle 1 rad; pair 16: 1 / 10000^(32/64) = 0.01 rad
+    np.testing.assert_allclose(got[1, 0].ravel(), [np.cos(1.0), -np.sin(1.0), np.sin(1.0), np.cos(1.0)],
+                               atol=1e-6)
+    np.testing.assert_allclose(got[1, 16, 1, 0], np.sin(0.01), atol=1e-7)
 
 
 def test_gqa_helper():

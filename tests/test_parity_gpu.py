@@ -255,6 +255,54 @@ def test_rms_rope_split_half_kernel(ex):
     np.testing.assert_allclose(out2.float().cpu().numpy(), ora.to_fp16_storage(ref2), atol=4e-3, rtol=2e-3)
 
 
+# ------------------------------------------- head_dim 64 (the LLM adapter) --
+@pytest.mark.parametrize("target,context", [(512, None), (300, None), (512, 512), (300, 77), (1, 512)])
+@pytest.mark.parametrize("layout", ["token", "head"])
+def test_adapter_attention_d64(ex, target, context, layout):
+    """LLMAdapterMetal.swift:361-404: 16 heads of 64, rms_rope_adapter64 on q
+    and k (fused here), non-causal self- or cross-attention."""
+    case = inputs.adapter_attention(seed=target + (context or 0), target_tokens=target,
+                                    context_tokens=context)
+    out = run_case(ex, case, layout=layout)
+    assert_parity(out, case.oracle(), what=f"adapter {target}x{context} {layout}")
+
+
+@pytest.mark.parametrize("s,causal", [(1, False), (129, True), (300, False), (640, True)])
+def test_d64_ragged_and_causal(ex, s, causal):
+    q, k, v = inputs.draw_qkv(300 + s, (2, s, 3, 64), (2, s, 3, 64))
+    case = inputs.Case(f"d64_{s}", q, k, v, qk_norm="rms_rope",
+                       rope_table=ora.adapter_rope_table(s), causal=causal)
+    out = run_case(ex, case)
+    assert_parity(out, case.oracle(), what=f"d64 S={s} causal={causal}")
+
+
+def test_d64_gqa_and_padding(ex):
+    q, k, v = inputs.draw_qkv(77, (1, 257, 8, 64), (1, 400, 2, 64))
+    case = inputs.Case("d64_gqa_pad", q, k, v, qk_norm="rms", kv_valid_len=[333])
+    out = run_case(ex, case)
+    assert_parity(out, case.oracle(), what="d64 GQA 8q/2kv, valid 333 of 400")
+    case = inputs.Case("d64_gqa", q, k, v)
+    out = run_case(ex, case, layout="head")
+    assert_parity(out, case.oracle(), what="d64 GQA, no norm, head-major")
+
+
+def test_rms_rope_adapter64_kernel(ex):
+    """rms_rope_adapter64 (AnimaKernels.metal:733-763) through the standalone
+    rms_rope_split_half entry at head_dim 64, with a non-trivial weight."""
+    import torch
+    case = inputs.adapter_attention(seed=5, target_tokens=200, heads=16)
+    x = to_dev(case.q[0])  # [S, H, 64]
+    w = torch.linspace(0.5, 1.5, 64).half().cuda()
+    rope = to_dev(case.rope_table)
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    ex.rms_rope_split_half(stream, x, out, w, rope, tokens=200, heads=16, head_dim=64)
+    torch.cuda.synchronize()
+    ref = ora.apply_split_half_rope(ora.rms_norm_heads(case.q.astype(np.float32), w.float().cpu().numpy()),
+                                    case.rope_table)[0]
+    np.testing.assert_allclose(out.float().cpu().numpy(), ora.to_fp16_storage(ref), atol=4e-3, rtol=2e-3)
+
+
 def test_rejects_unsupported(ex):
     """AttentionExecutorTests.swift:404-423 and :536-562."""
     import torch
