@@ -67,7 +67,7 @@ class AttnDesc(ctypes.Structure):
         ("kv_valid_lens", ctypes.c_void_p),
         ("scale", ctypes.c_float), ("qk_norm", ctypes.c_int32), ("eps", ctypes.c_float),
         ("q_norm_weight", ctypes.c_void_p), ("k_norm_weight", ctypes.c_void_p),
-        ("rope_table", ctypes.c_void_p), ("rope_rows", ctypes.c_int32), ("reserved0", ctypes.c_int32),
+        ("rope_table", ctypes.c_void_p), ("rope_rows", ctypes.c_int32), ("qk_norm_targets", ctypes.c_int32),
         ("q_bytes", ctypes.c_int64), ("k_bytes", ctypes.c_int64), ("v_bytes", ctypes.c_int64),
         ("o_bytes", ctypes.c_int64),
     ]

@@ -180,6 +180,9 @@ int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "eps must be finite and >= 0");
   if (d->qk_norm < ANIMAXS_QK_NONE || d->qk_norm > ANIMAXS_QK_RMS_ROPE)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown qk_norm mode %d", d->qk_norm);
+  if (d->qk_norm_targets < ANIMAXS_QK_NORM_BOTH || d->qk_norm_targets > ANIMAXS_QK_NORM_K_ONLY)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown qk_norm_targets %d",
+                        d->qk_norm_targets);
   if (d->qk_norm == ANIMAXS_QK_RMS_ROPE) {
     if (d->rope_table == nullptr)
       return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "qk_norm RMS_ROPE needs a rope table");
@@ -360,18 +363,28 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     jk.batch = d->batch;
     jk.weight = static_cast<const __half*>(d->k_norm_weight);
     jk.rows = static_cast<int64_t>(d->batch) * d->kv_len * kv_count;
-    np.njobs = 2;
+    // The caller may hold an already normalised q or k (qk_norm_targets).
+    const bool norm_q = d->qk_norm_targets != ANIMAXS_QK_NORM_K_ONLY;
+    const bool norm_k = d->qk_norm_targets != ANIMAXS_QK_NORM_Q_ONLY;
+    const NormJob q_job = jq, k_job = jk;
+    np.njobs = 0;
+    if (norm_q) np.job[np.njobs++] = q_job;
+    if (norm_k) np.job[np.njobs++] = k_job;
     np.status = ctx->d_status;
     cudaError_t e = ax::launch_qk_norm(np, stream);
     if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "qk_norm launch");
-    qa = qn;
-    ka = kn;
-    q_st = jq.out_tok;
-    q_sh = D;
-    q_sb = jq.out_batch;
-    k_st = jk.out_tok;
-    k_sh = D;
-    k_sb = jk.out_batch;
+    if (norm_q) {
+      qa = qn;
+      q_st = q_job.out_tok;
+      q_sh = D;
+      q_sb = q_job.out_batch;
+    }
+    if (norm_k) {
+      ka = kn;
+      k_st = k_job.out_tok;
+      k_sh = D;
+      k_sb = k_job.out_batch;
+    }
   }
 
   CUtensorMap tq, tk, tv;

@@ -126,16 +126,26 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
     jk.batch = d->batch;
     jk.weight = static_cast<const __half*>(d->k_norm_weight);
     jk.rows = static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads;
-    np.njobs = 2;
+    // The caller may hold an already normalised q or k (qk_norm_targets).
+    const bool norm_q = d->qk_norm_targets != ANIMAXS_QK_NORM_K_ONLY;
+    const bool norm_k = d->qk_norm_targets != ANIMAXS_QK_NORM_Q_ONLY;
+    const ax::NormJob q_job = jq, k_job = jk;
+    np.njobs = 0;
+    if (norm_q) np.job[np.njobs++] = q_job;
+    if (norm_k) np.job[np.njobs++] = k_job;
     if (ax::launch_qk_norm(np, stream) != cudaSuccess) return ANIMAXS_ERR_CUDA;
-    qa = qn;
-    ka = kn;
-    q_st = jq.out_tok;
-    q_sh = D;
-    q_sb = jq.out_batch;
-    k_st = jk.out_tok;
-    k_sh = D;
-    k_sb = jk.out_batch;
+    if (norm_q) {
+      qa = qn;
+      q_st = q_job.out_tok;
+      q_sh = D;
+      q_sb = q_job.out_batch;
+    }
+    if (norm_k) {
+      ka = kn;
+      k_st = k_job.out_tok;
+      k_sh = D;
+      k_sb = k_job.out_batch;
+    }
   }
 
   CUtensorMap tq, tk, tv;

@@ -35,6 +35,8 @@ from ._lib import (AttentionValidationError, AttnDesc, QK_NONE, QK_RMS, QK_RMS_R
 NUMERICS = ("legacy", "fp32ScoresAndSoftmax", "bf16_compute")
 BACKENDS = ("legacyHeadMajorMPS", "stridedTokenMajorMPS", "streamingMPS", "metalFlash")
 _QK = {"none": QK_NONE, "rms": QK_RMS, "rms_rope": QK_RMS_ROPE}
+# animaxs_qk_norm_targets: which of q and k the qk_norm mode applies to.
+_QK_TARGETS = {"both": 0, "q": 1, "k": 2}
 
 
 @dataclass(frozen=True)
@@ -163,7 +165,8 @@ class AttentionExecutor:
     def make_desc(self, *, heads, query_count, key_count, head_dim, key_value_heads=None,
                   causal=False, layout=None, qk_norm="none", q_norm_weight=None,
                   k_norm_weight=None, rope_table=None, eps=1e-6, kv_valid_len=None,
-                  kv_valid_lens=None, scale=None, batch=1, lengths=(0, 0, 0, 0)) -> AttnDesc:
+                  kv_valid_lens=None, scale=None, batch=1, lengths=(0, 0, 0, 0),
+                  qk_norm_targets="both") -> AttnDesc:
         kv_heads = heads if key_value_heads is None else key_value_heads
         layout = self.layout if layout is None else layout
         if layout.is_token_major:
@@ -204,6 +207,10 @@ class AttentionExecutor:
         if qk_norm not in _QK:
             raise AttentionValidationError(_lib.ERR_INVALID_ARG, f"unknown qk_norm {qk_norm!r}")
         d.qk_norm = _QK[qk_norm]
+        if qk_norm_targets not in _QK_TARGETS:
+            raise AttentionValidationError(_lib.ERR_INVALID_ARG,
+                                           f"unknown qk_norm_targets {qk_norm_targets!r}")
+        d.qk_norm_targets = _QK_TARGETS[qk_norm_targets]
         d.eps = float(eps)
         d.q_norm_weight = None if q_norm_weight is None else _ptr_len(q_norm_weight)[0]
         d.k_norm_weight = None if k_norm_weight is None else _ptr_len(k_norm_weight)[0]
@@ -237,13 +244,13 @@ class AttentionExecutor:
 
     def strided_desc(self, q, k, v, out, *, causal=False, qk_norm="none", rope_table=None,
                      q_norm_weight=None, k_norm_weight=None, eps=1e-6, kv_valid_len=None,
-                     kv_valid_lens=None, scale=None) -> AttnDesc:
+                     kv_valid_lens=None, scale=None, qk_norm_targets="both") -> AttnDesc:
         """Descriptor for ``[B, S, H, D]`` tensors (D 128 or 64) with arbitrary strides (cached)."""
         key = (q.shape, k.shape, q.stride(), k.stride(), v.stride(), out.stride(), causal, qk_norm,
                None if rope_table is None else (rope_table.data_ptr(), rope_table.numel()),
                None if q_norm_weight is None else q_norm_weight.data_ptr(),
                None if k_norm_weight is None else k_norm_weight.data_ptr(), eps, kv_valid_len,
-               None if kv_valid_lens is None else kv_valid_lens.data_ptr(), scale)
+               None if kv_valid_lens is None else kv_valid_lens.data_ptr(), scale, qk_norm_targets)
         desc = self._desc_cache.get(key)
         if desc is None:
             b, sq, h, d = q.shape
@@ -253,7 +260,8 @@ class AttentionExecutor:
                                   layout=AttentionInputLayout.head_major, qk_norm=qk_norm,
                                   q_norm_weight=q_norm_weight, k_norm_weight=k_norm_weight,
                                   rope_table=rope_table, eps=eps, kv_valid_len=kv_valid_len,
-                                  kv_valid_lens=kv_valid_lens, scale=scale, batch=b)
+                                  kv_valid_lens=kv_valid_lens, scale=scale, batch=b,
+                                  qk_norm_targets=qk_norm_targets)
             for name, t in (("q", q), ("k", k), ("v", v), ("o", out)):
                 sb, st, sh, sd = t.stride()
                 if sd != 1:
@@ -270,7 +278,8 @@ class AttentionExecutor:
         """Strided entry: ``q``/``out`` are ``[B, Sq, H, D]`` and ``k``/``v``
         ``[B, Sk, Hkv, D]`` fp16 device tensors, D 128 or 64, with ANY strides (token-major,
         head-major views, batch gaps).  Keywords: ``causal``, ``qk_norm``
-        (``"none"``/``"rms"``/``"rms_rope"``), ``rope_table``, ``q_norm_weight``,
+        (``"none"``/``"rms"``/``"rms_rope"``), ``qk_norm_targets`` (``"both"``, or
+        ``"q"`` when k is already normalised, e.g. a cached cross K), ``rope_table``, ``q_norm_weight``,
         ``k_norm_weight``, ``eps``, ``kv_valid_len``, ``kv_valid_lens``, ``scale``.
         Enqueues on ``stream`` (default: the current torch stream); returns ``out``."""
         import torch

@@ -71,6 +71,17 @@ typedef enum animaxs_qk_norm {
   ANIMAXS_QK_RMS_ROPE = 2
 } animaxs_qk_norm;
 
+/* Which of q and k the qk_norm mode is applied to.  Q_ONLY serves callers that
+ * keep k already normalised, such as the cross-K/V cache (CrossKVCache,
+ * DiTBlockExecutor.swift:19-43; cached post-RMSNorm K reused across steps at
+ * :1105-1161): normalise K once with animaxs_rmsnorm_heads_half, then pass it
+ * with Q_ONLY.  0 (BOTH) is the zero-initialised default. */
+typedef enum animaxs_qk_norm_targets {
+  ANIMAXS_QK_NORM_BOTH = 0,
+  ANIMAXS_QK_NORM_Q_ONLY = 1,
+  ANIMAXS_QK_NORM_K_ONLY = 2
+} animaxs_qk_norm_targets;
+
 /* One attention call.  Replaces the argument list of
  * AttentionExecutor.encode(commandBuffer:query:queryOffset:key:...:heads:
  * queryCount:keyCount:headDim:keyValueHeads:causal:probe:layout:)
@@ -102,7 +113,7 @@ typedef struct animaxs_attn_desc {
   const float* rope_table;   /* DEVICE fp32[rope_rows][head_dim/2][2][2] blocks [cos,-sin,sin,cos];
                                 row = token index; RMS_ROPE only */
   int32_t rope_rows;         /* rows in rope_table; must be >= max(q_len, kv_len) */
-  int32_t reserved0;
+  int32_t qk_norm_targets;   /* animaxs_qk_norm_targets; 0 = q and k */
   /* Optional extents (bytes from the pointer passed to the call) used for the
    * reference's range validation (:808-823); 0 = not checked. */
   int64_t q_bytes, k_bytes, v_bytes, o_bytes;

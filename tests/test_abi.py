@@ -95,6 +95,10 @@ def test_validation_mirrors_reference(lib):
     assert _validate(lib, _desc(lib, kv_valid_len=1025)) == -1
     assert _validate(lib, _desc(lib, kv_valid_len=-1)) == -1
     assert _validate(lib, _desc(lib, scale=-1.0)) == -1
+    # normalisation targets (q and k / q only / k only)
+    for t in (0, 1, 2):
+        assert _validate(lib, _desc(lib, qk_norm_targets=t)) == 0
+    assert _validate(lib, _desc(lib, qk_norm_targets=3)) == -1
     assert _validate(lib, _desc(lib, qk_norm=2)) == -1            # rope table missing
     assert _validate(lib, _desc(lib, qk_norm=2, rope_table=0x5000, rope_rows=1023)) == -1
     assert _validate(lib, _desc(lib, qk_norm=2, rope_table=0x5000, rope_rows=1024)) == 0

@@ -255,6 +255,34 @@ def test_rms_rope_split_half_kernel(ex):
     np.testing.assert_allclose(out2.float().cpu().numpy(), ora.to_fp16_storage(ref2), atol=4e-3, rtol=2e-3)
 
 
+def test_cached_cross_k_matches_fused(ex):
+    """The cross-K/V cache flow (DiTBlockExecutor.swift:1105-1161): K normalised
+    once (rmsnorm_heads_half) and reused, q normalised per call
+    (qk_norm_targets="q"), must equal the fused q-and-k call bit for bit."""
+    import torch
+    case = inputs.dit_cross(seed=21, q_len=640, kv_len=512, heads=4, kv_valid=None)
+    q, k, v = to_dev(case.q), to_dev(case.k), to_dev(case.v)
+    wq = torch.linspace(0.8, 1.2, 128).half().cuda()
+    wk = torch.linspace(1.2, 0.8, 128).half().cuda()
+    fused = ex.attention(q, k, v, qk_norm="rms", q_norm_weight=wq, k_norm_weight=wk)
+    k_cached = torch.empty_like(k)
+    ex.rmsnorm_heads_half(torch.cuda.current_stream(), k[0], k_cached[0], wk, tokens=512, heads=4)
+    cached = ex.attention(q, k_cached, v, qk_norm="rms", q_norm_weight=wq, qk_norm_targets="q")
+    torch.cuda.synchronize()
+    assert torch.equal(fused, cached)
+    # and k-only: q pre-normalised by the caller
+    q_norm = torch.empty_like(q)
+    ex.rmsnorm_heads_half(torch.cuda.current_stream(), q[0], q_norm[0], wq, tokens=640, heads=4)
+    konly = ex.attention(q_norm, k, v, qk_norm="rms", k_norm_weight=wk, qk_norm_targets="k")
+    torch.cuda.synchronize()
+    assert torch.equal(fused, konly)
+    assert_parity(fused.float().cpu().numpy(),
+                  ora.forward(case.q, case.k, case.v, qk_norm="rms",
+                              q_norm_weight=wq.float().cpu().numpy(),
+                              k_norm_weight=wk.float().cpu().numpy()),
+                  what="cross with norm weights")
+
+
 # ------------------------------------------- head_dim 64 (the LLM adapter) --
 @pytest.mark.parametrize("target,context", [(512, None), (300, None), (512, 512), (300, 77), (1, 512)])
 @pytest.mark.parametrize("layout", ["token", "head"])
