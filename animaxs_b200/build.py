@@ -17,7 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libanimaxs_attn.so")
-SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "qk_norm.cu", "sharded.cu", "noalloc.cu"]
+SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "attn_wide_sm100.cu", "qk_norm.cu", "sharded.cu",
+           "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
          "--expt-relaxed-constexpr", "-Xptxas", "-v"]

@@ -168,9 +168,10 @@ int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q
   if (d->batch <= 0 || d->heads <= 0 || d->q_len <= 0 || d->kv_len <= 0 || d->head_dim <= 0 ||
       d->kv_heads <= 0 || d->heads % d->kv_heads != 0 || (d->causal && d->q_len != d->kv_len))
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "%s", kShapeMsg);
-  if (d->head_dim != 128 && d->head_dim != 64)
+  const bool wide = d->head_dim == 256 || d->head_dim == 384;
+  if (d->head_dim != 128 && d->head_dim != 64 && !wide)
     return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
-                        "attention on B200 requires headDim 128 or 64 (got %d)", d->head_dim);
+                        "attention on B200 requires headDim 64, 128, 256 or 384 (got %d)", d->head_dim);
   if (d->kv_valid_len < 0 || d->kv_valid_len > d->kv_len)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
                         "kv_valid_len %d outside [0, keyCount %d]", d->kv_valid_len, d->kv_len);
@@ -183,6 +184,9 @@ int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q
   if (d->qk_norm_targets < ANIMAXS_QK_NORM_BOTH || d->qk_norm_targets > ANIMAXS_QK_NORM_K_ONLY)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown qk_norm_targets %d",
                         d->qk_norm_targets);
+  if (wide && d->qk_norm != ANIMAXS_QK_NONE)
+    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
+                        "fused q/k normalisation requires headDim 128 or 64 (got %d)", d->head_dim);
   if (d->qk_norm == ANIMAXS_QK_RMS_ROPE) {
     if (d->rope_table == nullptr)
       return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "qk_norm RMS_ROPE needs a rope table");

@@ -42,12 +42,11 @@
 #include <atomic>
 
 #include "kernels.h"
-#include "sm100_ptx.cuh"
+#include "flash_common.cuh"
 
 namespace ax {
 namespace {
 
-constexpr uint32_t kPanelBytes = 128 * 128;             // 128 rows x 128 B (64 fp16)
 // Ring depths.  A tile load measured ~4000 cycles from issue to arrival under
 // full load; two stages each cover it (a third V stage, which still fits in
 // 227 KiB, measured no faster).
@@ -89,13 +88,6 @@ constexpr uint32_t kColO = 256;  // O_A at kColO, O_B at kColO + HD
 constexpr uint32_t kIdescQK = idesc_f16_f32(128, 128, false);  // B = K tile, K-major
 template <int HD>
 constexpr uint32_t kIdescPV = idesc_f16_f32(128, HD, true);     // B = V tile, MN-major, N = HD
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled when max grows > 2^8
-// Of every 8 adjacent column pairs, this many take exp2 on the FMA pipe
-// (polynomial) and the rest on the MUFU pipe.
-#ifndef AX_POLY_PAIRS
-#define AX_POLY_PAIRS 2
-#endif
-constexpr int kPolyPairsPer8 = AX_POLY_PAIRS;
 // Register split (setmaxnreg): the kernel launches 3 warpgroups at the
 // compiler's per-thread count N (ptxas: 168); the two softmax warpgroups raise
 // theirs to AX_SOFTMAX_REGS and the MMA/TMA warpgroup lowers its to
@@ -104,40 +96,6 @@ constexpr int kPolyPairsPer8 = AX_POLY_PAIRS;
 // ptxas report before it links the library.
 #define AX_SOFTMAX_REGS 208
 #define AX_OTHER_REGS 88
-
-// 2^x on the FMA pipe for a pair of values.  Range reduction x = j + f with
-// j = round(x) obtained by adding 1.5*2^23 (the integer lands in the low
-// mantissa bits), f in [-1/2, 1/2]; 2^f by a degree-4 minimax polynomial
-// (relative error 3.6e-6, coefficients from gen_exp2_poly.py); 2^j by adding
-// j to the exponent field.  x is clamped at -126 so the result stays normal;
-// masked entries (-inf) come out as 2^-126, which is 0 once stored as fp16
-// and negligible in the fp32 row sum.
-__device__ __forceinline__ float2 ex2_poly2(float2 x) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  x.x = fmaxf(x.x, -126.0f);
-  x.y = fmaxf(x.y, -126.0f);
-  const float2 t = add2(x, make_float2(kMagic, kMagic));
-  const float2 j = add2(t, make_float2(-kMagic, -kMagic));
-  const float2 f = add2(x, make_float2(-j.x, -j.y));
-  float2 p = fma2(make_float2(0.009782912209630013f, 0.009782912209630013f), f,
-                  make_float2(0.055976882576942444f, 0.055976882576942444f));
-  p = fma2(p, f, make_float2(0.24020710587501526f, 0.24020710587501526f));
-  p = fma2(p, f, make_float2(0.6931136250495911f, 0.6931136250495911f));
-  p = fma2(p, f, make_float2(1.0f, 1.0f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
-
-// K-major operand (rows x 128 fp16 as two 64-column SW128 panels): k-step kk
-// (16 columns) starts in panel kk/4 at byte (kk%4)*32.
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int kk) {
-  return sw128_desc(tile + (kk >> 2) * kPanelBytes + (kk & 3) * 32, 16, 1024);
-}
-// MN-major V operand: k-step kk covers keys [16kk, 16kk+16) = 2 groups of 8
-// rows (1024 B apart); the two 64-wide head_dim panels are kPanelBytes apart.
-__device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile, int kk) {
-  return sw128_desc(tile + kk * 2048, kPanelBytes, 1024);
-}
 
 // Descriptors advance by constant offsets of their start-address field
 // (bits 0-13, address >> 4; every operand lies below 256 KiB of shared memory,
@@ -576,7 +534,7 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
   if (e != cudaSuccess) return e;
   if (p.head_dim == 64) return launch_hd<64>(tq, tk, tv, p, heads_in_launch, batch, dev, stream);
   if (p.head_dim == 128) return launch_hd<128>(tq, tk, tv, p, heads_in_launch, batch, dev, stream);
-  return cudaErrorInvalidValue;
+  return launch_attn_wide(tq, tk, tv, p, heads_in_launch, batch, dev, stream);
 }
 
 }  // namespace ax

@@ -8,21 +8,22 @@
 
 namespace ax {
 
-// Parameters of the flash-attention kernel (attn_fwd_sm100.cu).  q/k/v arrive
+// Parameters of the flash-attention kernels (attn_fwd_sm100.cu, attn_wide_sm100.cu).  q/k/v arrive
 // through TMA tensor maps over [batch][head][token][head_dim] fp16 views (any
 // strides); the output is written with plain stores.
 struct AttnFwdParams {
-  int head_dim;          // 64 or 128
+  int head_dim;          // 64 or 128 (attn_fwd_sm100.cu), 256 or 384 (attn_wide_sm100.cu)
   int q_len;
   int kv_len;
   int heads_per_kv;      // heads / kv_heads (GQA group size)
   int kv_valid;          // keys >= kv_valid masked (already clamped to [1, kv_len])
   const int* kv_valid_dev;  // optional per-batch override (device)
   int causal;
-  int n_q_tiles;         // query-tile pairs per head: ceil(q_len / attn_fwd_rows_per_cta())
+  int n_q_tiles;         // query tiles per head: pairs (attn_fwd_rows_per_cta()) or, wide, 128-row tiles
   int head_offset;       // first query head handled by this launch
   int heads_in_launch;   // set by launch_attn_fwd: query heads of this launch
   int n_items;           // set by launch_attn_fwd: n_q_tiles * heads_in_launch * batch
+  int n_split;           // set by the wide launcher: CTAs (one cluster) sharing a query tile's keys
   int o_head_base;       // output head index = h - o_head_base
   float scale_log2;      // softmax scale * log2(e)
   __half* o;
@@ -61,7 +62,12 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
                             const AttnFwdParams& p, int heads_in_launch, int batch,
                             cudaStream_t stream);
 
-int attn_fwd_rows_per_cta();  // query rows one attention CTA covers
+// Head dims 256 / 384 (called by launch_attn_fwd).
+cudaError_t launch_attn_wide(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const AttnFwdParams& p, int heads_in_launch, int batch, int dev,
+                             cudaStream_t stream);
+
+int attn_fwd_rows_per_cta();  // query rows one attention CTA covers (head dims 64 / 128)
 
 cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
 

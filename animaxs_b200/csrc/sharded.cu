@@ -185,6 +185,9 @@ extern "C" int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_
   if (d->heads % world != 0)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "heads (%d) must be a multiple of world (%d)",
                         d->heads, world);
+  if (d->head_dim != 64 && d->head_dim != 128)
+    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
+                        "head-sharded attention requires headDim 128 or 64 (got %d)", d->head_dim);
   const int hr = d->heads / world;  // every rank reads the full K/V, so any GQA grouping works
   NcclApi* api = nccl();
   if (api == nullptr) return ax_set_error(ctx, ANIMAXS_ERR_NCCL, "libnccl.so.2 not loadable");

@@ -245,7 +245,7 @@ class AttentionExecutor:
     def strided_desc(self, q, k, v, out, *, causal=False, qk_norm="none", rope_table=None,
                      q_norm_weight=None, k_norm_weight=None, eps=1e-6, kv_valid_len=None,
                      kv_valid_lens=None, scale=None, qk_norm_targets="both") -> AttnDesc:
-        """Descriptor for ``[B, S, H, D]`` tensors (D 128 or 64) with arbitrary strides (cached)."""
+        """Descriptor for ``[B, S, H, D]`` tensors (D 64, 128, 256 or 384) with arbitrary strides (cached)."""
         key = (q.shape, k.shape, q.stride(), k.stride(), v.stride(), out.stride(), causal, qk_norm,
                None if rope_table is None else (rope_table.data_ptr(), rope_table.numel()),
                None if q_norm_weight is None else q_norm_weight.data_ptr(),
@@ -276,7 +276,7 @@ class AttentionExecutor:
 
     def attention(self, q, k, v, out=None, *, stream=None, **kw):
         """Strided entry: ``q``/``out`` are ``[B, Sq, H, D]`` and ``k``/``v``
-        ``[B, Sk, Hkv, D]`` fp16 device tensors, D 128 or 64, with ANY strides (token-major,
+        ``[B, Sk, Hkv, D]`` fp16 device tensors, D 64, 128, 256 or 384, with ANY strides (token-major,
         head-major views, batch gaps).  Keywords: ``causal``, ``qk_norm``
         (``"none"``/``"rms"``/``"rms_rope"``), ``qk_norm_targets`` (``"both"``, or
         ``"q"`` when k is already normalised, e.g. a cached cross K), ``rope_table``, ``q_norm_weight``,

@@ -95,8 +95,10 @@ typedef struct animaxs_attn_desc {
   int32_t kv_heads;     /* `keyValueHeads:`; query head h reads kv head h / (heads/kv_heads) */
   int32_t q_len;        /* `queryCount:` */
   int32_t kv_len;       /* `keyCount:` */
-  int32_t head_dim;     /* `headDim:`; this build runs 128 (DiT, Qwen) and 64 (LLM adapter,
-                           LLMAdapterMetal.swift:9-10,394-397); others -> UNSUPPORTED */
+  int32_t head_dim;     /* `headDim:`; this build runs 128 (DiT, Qwen), 64 (LLM adapter,
+                           LLMAdapterMetal.swift:9-10,394-397), 384 (VAE middle attention,
+                           VAEDecoder.swift:398-404: heads 1) and 256; others -> UNSUPPORTED.
+                           qk_norm other than NONE needs 128 or 64. */
   int64_t q_tok_stride, q_head_stride, q_batch_stride;
   int64_t k_tok_stride, k_head_stride, k_batch_stride;
   int64_t v_tok_stride, v_head_stride, v_batch_stride;
@@ -254,7 +256,8 @@ int animaxs_comm_destroy(animaxs_comm* comm);
 /* Rank `rank` of `world` computes query heads [rank*heads/world, (rank+1)*heads/world)
  * of `desc` (q/k/v/o pointers are the FULL tensors, identical on every rank),
  * then one ncclAllGather assembles every rank's heads into `o`, so every rank
- * ends with the complete output.  heads must be a multiple of world. */
+ * ends with the complete output.  heads must be a multiple of world; head_dim
+ * 128 or 64. */
 int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_comm* comm,
                                       const animaxs_attn_desc* desc, const void* q,
                                       const void* k, const void* v, void* o, void* stream);

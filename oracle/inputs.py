@@ -5,7 +5,7 @@ TEST INFRASTRUCTURE ONLY (used by ``tests/``, ``smoke()`` and the CPU legs of
 this container, the GPU box and the golden-fixture script all see identical
 values: ``g = torch.Generator().manual_seed(seed)``; ``q, k, v = randn(...)``
 in that order as fp32, then rounded to fp16.  Shapes are token-major
-``[B, S, H, D]`` (D = 128; 64 for the LLM adapter) -- the layout the
+``[B, S, H, D]`` (D = 128; 64 for the LLM adapter; 384 for the VAE) -- the layout the
 reference's projections produce
 (``DiTBlockExecutor.swift:1097-1131``, ``QwenEncoderMetal.swift:245-262``).
 """
@@ -114,6 +114,16 @@ def adapter_attention(seed: int = 0, target_tokens: int = 512, context_tokens: i
     name = f"adapter_{target_tokens}x{kv}"
     return Case(name, q, k, v, qk_norm="rms_rope",
                 rope_table=ora.adapter_rope_table(max(target_tokens, kv)))
+
+
+def vae_attention(seed: int = 0, latent: int = 64, channels: int = 384, batch: int = 1) -> Case:
+    """The VAE decoder's middle attention (VAEDecoder.swift:351-410): one head
+    of ``channels`` over the ``latent x latent`` positions, non-causal, no q/k
+    norm, scale 1/sqrt(channels).  Q/K/V stand in for the normalised 1x1 to_qkv
+    projection of a latent (unit-variance per channel)."""
+    s = latent * latent
+    q, k, v = draw_qkv(seed, (batch, s, 1, channels), (batch, s, 1, channels))
+    return Case(f"vae_attn_{latent}x{latent}", q, k, v, meta={"seed": seed, "latent": latent})
 
 
 def workload_seed(prompt: int, step: int, block: int) -> int:

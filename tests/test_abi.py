@@ -84,6 +84,11 @@ def test_validation_mirrors_reference(lib):
     assert _validate(lib, _desc(lib, head_dim=64)) == 0
     assert _validate(lib, _desc(lib, head_dim=96)) == -2
     assert _validate(lib, _desc(lib, head_dim=32)) == -2
+    # VAE middle attention: one head of 384 (VAEDecoder.swift:351-410); 256 shares its kernel.
+    assert _validate(lib, _desc(lib, heads=1, kv_heads=1, head_dim=384)) == 0
+    assert _validate(lib, _desc(lib, head_dim=256)) == 0
+    assert _validate(lib, _desc(lib, head_dim=512)) == -2
+    assert _validate(lib, _desc(lib, head_dim=384, qk_norm=1)) == -2  # fused norm: 64 / 128 only
     # null and misaligned buffers, misaligned stride
     assert _validate(lib, ok, (0, 0x2000, 0x3000, 0x4000)) == -1
     assert _validate(lib, ok, (0x1008, 0x2000, 0x3000, 0x4000)) == -1
