@@ -261,10 +261,10 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [batch][heads][rows][dim] fp16 view (dim 64 or 128); box = 64 columns x 128
-// rows, 128B swizzle.
+// [batch][heads][rows][dim] fp16 view (dim a multiple of 64); box = 64 columns x
+// box_rows rows, 128B swizzle.
 int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int64_t dim, int64_t rows,
-                 int64_t heads, int64_t batch, int64_t st, int64_t sh, int64_t sb) {
+                 int64_t heads, int64_t batch, int64_t st, int64_t sh, int64_t sb, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr)
     return ax_set_error(ctx, ANIMAXS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
@@ -276,7 +276,7 @@ int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int6
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(rows > 1 ? st * 2 : fallback),
                            static_cast<cuuint64_t>(heads > 1 ? sh * 2 : fallback),
                            static_cast<cuuint64_t>(batch > 1 ? sb * 2 : fallback)};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

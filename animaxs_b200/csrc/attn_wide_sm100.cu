@@ -9,21 +9,23 @@
 // O = softmax(Q K^T * scale + mask) V with fp32 statistics, online over 128-key
 // tiles.
 //
-// One CTA owns one 128-row query tile.  A 384-wide tile does not fit twice in
-// TMEM beside its score tile, so the layout is S [0,128) (P overlays its first
-// 64 columns) and O [128, 128+HD): 512 columns at HD 384.  Q stays resident in
-// shared memory (HD/128 chunks of 128x128); K and V stream through one 4-stage
-// ring of 128-key x 128-column chunks: for each key tile, K chunks 0..HD/128-1
-// (S accumulates over them), then V chunks (chunk c feeds O columns
-// [128c, 128c+128)).  Ten warps:
+// One CTA owns one 128-row query tile.  A 384-wide O does not fit twice in
+// TMEM beside a score tile, so TMEM holds S [0,128) and O [128, 128+HD) (512
+// columns at HD 384), and P goes to shared memory (a 128x128 fp16 K-major
+// tile, the A operand of PV).  That frees S as soon as the softmax has read it:
+// the MMA warp issues QK(j+1) while the softmax still computes P(j), then
+// PV(j), so the tensor core runs QK(j+1), PV(j), QK(j+2), PV(j+1), ... and
+// the softmax hides under the QKs.  Q stays resident in shared memory
+// (HD/128 chunks of 128x128); K and V stream through one ring of 128-key x
+// 128-column chunks in the order the MMAs consume them: K(0), then per tile j
+// K(j+1) (S accumulates over the head-dim chunks) and V(j) (chunk c feeds O
+// columns [128c, 128c+128)).  Ten warps:
 //   warps 0-3 / 4-7  softmax: warpgroup g takes keys [64g, 64g+64) of every S
-//                    tile and O columns [g*HD/2, (g+1)*HD/2); thread t owns query
-//                    row t (TMEM lane t).  The two halves of a row exchange their
-//                    maxima through shared memory behind a named barrier.
+//                    tile (= P panel g) and O columns [g*HD/2, (g+1)*HD/2);
+//                    thread t owns query row t (TMEM lane t).  The two halves
+//                    of a row exchange their maxima through shared memory.
 //   warp 8           MMA issuer + TMEM owner.
 //   warp 9           TMA producer.
-// With a single S buffer the tensor core idles while the softmax runs
-// (~20% of a 3072-cycle MMA tile at HD 384).
 //
 // Key split.  A 4096-position VAE image has 32 query tiles: one CTA each would
 // leave 116 of 148 SMs idle.  When there are few query tiles the launch splits
@@ -37,43 +39,44 @@
 // then (the first cluster barrier follows every CTA's last MMA and copy).
 #include <atomic>
 
-#include "kernels.h"
+#include "api_internal.h"
 #include "flash_common.cuh"
+#include "kernels.h"
 
 namespace ax {
 namespace {
 
 constexpr int kThreads = 320;                  // 2 softmax warpgroups, MMA warp, TMA warp
 constexpr int kSoftmaxThreads = 256;
-constexpr int kStages = 4;                     // K/V chunk ring
 constexpr uint32_t kChunk = 2 * kPanelBytes;   // 128 rows x 128 fp16 = two SW128 panels (32 KiB)
 
 template <int HD>
 struct WideSmem {
   static constexpr int kNC = HD / 128;                   // 128-column chunks of the head dim
+  static constexpr int kStages = HD == 384 ? 3 : 4;      // K/V chunk ring (what 227 KiB leaves)
   static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kRing = kNC * kChunk;
+  static constexpr uint32_t kP = kNC * kChunk;           // P: 128 rows x 128 keys, K-major SW128
+  static constexpr uint32_t kRing = kP + kChunk;
   static constexpr uint32_t kBar = kRing + kStages * kChunk;
-  static constexpr uint32_t kStats = kBar - 4096;        // merge: (m, l) per rank and row (overlays the ring)
   static constexpr uint32_t kXch = kBar + 256;           // 2 x 128 floats: row max / row sum exchange
   static constexpr uint32_t kBytes = kXch + 1024 + 1024; // + alignment slack
 };
-// Merge receive buffer at offset 0: [sender rank][row][W + 4] fp32, W = HD / n_split
-// (the 4-float pad makes the per-row v4 stores and loads conflict-free).
-constexpr uint32_t recv_bytes(int hd, int ns) { return ns * 128u * (hd / ns + 4) * 4u; }
+constexpr int kMaxStages = 4;
 static_assert(WideSmem<384>::kBytes <= 227 * 1024, "shared memory exceeds the 227 KiB opt-in");
-static_assert(recv_bytes(384, 4) <= WideSmem<384>::kStats && recv_bytes(384, 2) <= WideSmem<384>::kStats,
-              "merge buffers overlap the statistics");
-static_assert(recv_bytes(256, 4) <= WideSmem<256>::kStats && recv_bytes(256, 2) <= WideSmem<256>::kStats,
-              "merge buffers overlap the statistics");
+// Merge buffers (offset 0): receive 128 x HD fp32, statistics 1 KiB, one 32-row
+// fp16 store stage; the ns == 1 store stage (128 x HD fp16) is smaller.
+static_assert(128u * 384 * 4 + 1024 + 32 * 384 * 2 <= WideSmem<384>::kBar, "merge buffers overflow");
+static_assert(128u * 256 * 4 + 1024 + 32 * 256 * 2 <= WideSmem<256>::kBar, "merge buffers overflow");
 
 enum : int {
   kBarQ = 0,
-  kBarFull = 1,                    // +stage
-  kBarEmpty = kBarFull + kStages,  // +stage
-  kBarSFull = kBarEmpty + kStages, // S of the current tile in TMEM
-  kBarPFull,                       // 256 arrivals: P of the current tile in TMEM
-  kBarODone,                       // the last PV retired
+  kBarFull = 1,                       // +stage
+  kBarEmpty = kBarFull + kMaxStages,  // +stage
+  kBarSFull = kBarEmpty + kMaxStages, // S(j) in TMEM
+  kBarSFree,                          // the softmax holds S(j) in registers: QK(j+1) may overwrite it
+  kBarPFull,                          // 256 arrivals: P(j) in shared memory
+  kBarPFree,                          // PV(j) retired: P may be rewritten, O rescaled
+  kBarODone,                          // the last PV retired
   kBarDone,
   kNumBars
 };
@@ -84,7 +87,7 @@ static_assert(kSlotAbort + 4 <= 256, "barrier block overflows its 256 bytes");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 128;
 constexpr uint32_t kIdescQK = idesc_f16_f32(128, 128, false);  // B = K chunk, K-major
-constexpr uint32_t kIdescPV = idesc_f16_f32(128, 128, true);   // B = V chunk, MN-major
+constexpr uint32_t kIdescPV = idesc_f16_f32(128, 128, true);   // A = P (K-major), B = V chunk, MN-major
 
 // Named barrier id of the two softmax warpgroups (0 is __syncthreads').
 constexpr uint32_t kSoftmaxBar = 1;
@@ -113,14 +116,15 @@ template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_wide_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const AttnFwdParams p) {
+                           const __grid_constant__ CUtensorMap tm_v,
+                           const __grid_constant__ CUtensorMap tm_o, const AttnFwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   using L = WideSmem<HD>;
   constexpr int NC = L::kNC;
-  const uint32_t sQ = base + L::kQ, sRing = base + L::kRing;
+  const uint32_t sQ = base + L::kQ, sP = base + L::kP, sRing = base + L::kRing;
   const uint32_t bar0 = base + L::kBar;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kBar + kSlotTmem);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kBar + kSlotAbort);
@@ -159,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
   }
   tc_fence_before();
   __syncthreads();
@@ -168,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 9) {
     // ------------------------------------------------------------ producer --
     if (lane == 0 && n_my > 0) {
-      int armed_q = 0, armed[kStages] = {};
+      int armed_q = 0, armed[kMaxStages] = {};
       bool ok = true;
       mbar_arrive_expect_tx(BAR(kBarQ), NC * kChunk);
 #pragma unroll
@@ -178,25 +183,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       armed_q = 1;
       uint32_t g = 0;  // chunks loaded so far: stage g % kStages
-      for (int j = 0; ok && j < n_my; ++j) {
-        const int key0 = (j_begin + j) * kTileN;
-        for (int kv = 0; ok && kv < 2; ++kv) {  // K chunks, then V chunks
-          const CUtensorMap* tm = kv ? &tm_v : &tm_k;
-          for (int c = 0; c < NC; ++c, ++g) {
-            const uint32_t st = g % kStages;
-            if (!(ok = mbar_wait(BAR(kBarEmpty + st), ((g / kStages) & 1u) ^ 1u, abort_flag, p.status)))
-              break;
-            const uint32_t dst = sRing + st * kChunk;
-            mbar_arrive_expect_tx(BAR(kBarFull + st), kChunk);
-            tma_load_4d(dst, tm, BAR(kBarFull + st), 128 * c, key0, kvh, b);
-            tma_load_4d(dst + kPanelBytes, tm, BAR(kBarFull + st), 128 * c + 64, key0, kvh, b);
-            ++armed[st];
-          }
+      // The NC chunks of key tile `jt` of K or V, in ring order.
+      auto load_tile = [&](const CUtensorMap* tm, int jt) {
+        const int key0 = (j_begin + jt) * kTileN;
+        for (int c = 0; c < NC; ++c, ++g) {
+          const uint32_t st = g % L::kStages;
+          if (!(ok = mbar_wait(BAR(kBarEmpty + st), ((g / L::kStages) & 1u) ^ 1u, abort_flag, p.status)))
+            return;
+          const uint32_t dst = sRing + st * kChunk;
+          mbar_arrive_expect_tx(BAR(kBarFull + st), kChunk);
+          tma_load_4d(dst, tm, BAR(kBarFull + st), 128 * c, key0, kvh, b);
+          tma_load_4d(dst + kPanelBytes, tm, BAR(kBarFull + st), 128 * c + 64, key0, kvh, b);
+          ++armed[st];
         }
+      };
+      // The order the MMA warp consumes them: K(0), then K(j+1), V(j).
+      load_tile(&tm_k, 0);
+      for (int j = 0; ok && j < n_my; ++j) {
+        if (j + 1 < n_my) load_tile(&tm_k, j + 1);
+        if (ok) load_tile(&tm_v, j);
       }
       // Never leave with a tensor copy still landing in shared memory.
       if (armed_q) mbar_wait_drain(BAR(kBarQ), 0);
-      for (int st = 0; st < kStages; ++st)
+      for (int st = 0; st < L::kStages; ++st)
         if (armed[st]) mbar_wait_drain(BAR(kBarFull + st), (armed[st] - 1) & 1);
     }
     __syncwarp();
@@ -206,11 +215,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (n_my > 0) {
       bool ok = mbar_wait_warp(BAR(kBarQ), 0, abort_flag, p.status);
       uint32_t g = 0;  // chunks consumed so far
-      for (int j = 0; ok && j < n_my; ++j) {
-        // S = Q K_j^T, accumulated over the head-dim chunks.
+      // S = Q K_jt^T, accumulated over the head-dim chunks.
+      auto qk = [&]() {
         for (int c = 0; c < NC; ++c, ++g) {
-          const uint32_t st = g % kStages;
-          if (!(ok = mbar_wait_warp(BAR(kBarFull + st), (g / kStages) & 1u, abort_flag, p.status))) break;
+          const uint32_t st = g % L::kStages;
+          if (!(ok = mbar_wait_warp(BAR(kBarFull + st), (g / L::kStages) & 1u, abort_flag, p.status)))
+            return;
           tc_fence_after();
           const uint64_t a0 = kmajor_desc(sQ + c * kChunk, 0);
           const uint64_t b0 = kmajor_desc(sRing + st * kChunk, 0);
@@ -221,23 +231,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_commit_warp(BAR(kBarEmpty + st));
         }
-        if (!ok) break;
         tc_commit_warp(BAR(kBarSFull));
-        // O[:, 128c:128c+128] += P V_j[:, 128c:128c+128]; P read from TMEM.
+      };
+      if (ok) qk();
+      for (int j = 0; ok && j < n_my; ++j) {
+        if (j + 1 < n_my) {
+          // QK(j+1) overwrites S once the softmax holds S(j) in registers.
+          if (!(ok = mbar_wait_warp(BAR(kBarSFree), j & 1u, abort_flag, p.status))) break;
+          tc_fence_after();
+          qk();
+          if (!ok) break;
+        }
+        // O[:, 128c:128c+128] += P(j) V_j[:, 128c:128c+128], P from shared memory.
         if (!(ok = mbar_wait_warp(BAR(kBarPFull), j & 1u, abort_flag, p.status))) break;
         tc_fence_after();
+        const uint64_t a0 = kmajor_desc(sP, 0);
         for (int c = 0; c < NC; ++c, ++g) {
-          const uint32_t st = g % kStages;
-          if (!(ok = mbar_wait_warp(BAR(kBarFull + st), (g / kStages) & 1u, abort_flag, p.status))) break;
+          const uint32_t st = g % L::kStages;
+          if (!(ok = mbar_wait_warp(BAR(kBarFull + st), (g / L::kStages) & 1u, abort_flag, p.status))) break;
           tc_fence_after();
           const uint64_t b0 = vmajor_desc(sRing + st * kChunk, 0);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ts_warp(tmem + kColO + 128 * c, tmem + kk * 8,
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t aoff = static_cast<uint64_t>(((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4);
+            umma_f16_ss_warp(tmem + kColO + 128 * c, a0 + aoff,
                              b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
                              (j > 0 || kk > 0) ? 1u : 0u);
+          }
           tc_commit_warp(BAR(kBarEmpty + st));
         }
+        if (!ok) break;
+        tc_commit_warp(BAR(kBarPFree));
       }
       if (ok) tc_commit_warp(BAR(kBarODone));
     }
@@ -251,14 +275,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x & 127;   // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + wg * 64;
-    const uint32_t p_addr = tmem + lane_base + wg * 32;
     const uint32_t o_addr = tmem + lane_base + kColO + wg * (HD / 2);
+    // Row t of P panel wg (keys [64wg, 64wg+64)); 16-byte unit u of a 128-byte
+    // SW128 row sits at unit u ^ (row % 8).
+    const uint32_t p_row = sP + wg * kPanelBytes + t * 128;
     const int row = q0 + t;
     const float sl2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_my; ++j) {
-      bool got = mbar_wait(BAR(kBarSFull), j & 1u, abort_flag, p.status);
+      bool got = ok && mbar_wait(BAR(kBarSFull), j & 1u, abort_flag, p.status);
+      // The other half read the previous tile's xch entry before its P(j-1) arrival.
+      if (got && j > 0) got = mbar_wait(BAR(kBarPFull), (j - 1) & 1u, abort_flag, p.status);
       got = __all_sync(0xffffffffu, got);
       uint32_t s[2][32];
       float pm = -INFINITY;
@@ -288,12 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         pm = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * sl2;
         xch[wg * 128 + t] = pm;
       }
-      // Both halves of every row must have read S before either writes P over
-      // S columns [0, 64); the barrier also makes the abort decision common.
+      // Every thread has S(j) in registers (and its max in xch); the barrier
+      // also makes the abort decision common.
       tc_fence_before();
       ok = softmax_bar_and(got);
-      tc_fence_after();
       if (!ok) break;
+      if (threadIdx.x == 0) mbar_arrive(BAR(kBarSFree));
       const float tmax = fmaxf(pm, xch[(wg ^ 1) * 128 + t]);
       const float m_new = fmaxf(m, tmax);
       const bool grow = m_new > m + kRescaleThreshold;  // also true on the first tile
@@ -301,18 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (grow) {
         l *= alpha;
         m = m_new;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // PV(j-1) precedes QK(j) in the MMA stream, so it has retired.
-#pragma unroll 1
-        for (int c4 = 0; c4 < HD / 64; ++c4) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c4 * 32, o);
-          tmem_ld_wait(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_addr + c4 * 32, o);
-        }
       }
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
       const float2 sl2v = make_float2(sl2, sl2);
@@ -335,12 +351,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
         pk[c >> 1] = pack_half2(pr.x, pr.y);
       }
-      tmem_st32(p_addr, pk);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(BAR(kBarPFull));
+      // PV(j-1) must have retired before P is rewritten and O rescaled.
+      bool free_p = true;
+      if (j > 0) {
+        free_p = mbar_wait(BAR(kBarPFree), (j - 1) & 1u, abort_flag, p.status);
+        free_p = __all_sync(0xffffffffu, free_p);
+      }
+      if (free_p) {
+        tc_fence_after();
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+          for (int c4 = 0; c4 < HD / 64; ++c4) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c4 * 32, o);
+            tmem_ld_wait(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_addr + c4 * 32, o);
+          }
+          tmem_st_wait();
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          st_shared_v4(p_row + ((u ^ (t & 7)) << 4), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        fence_proxy_async_smem();  // P is read by the tensor core (async proxy)
+        tc_fence_before();
+        mbar_arrive(BAR(kBarPFull));
+      }
       const float2 a = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
       l += a.x + a.y;
+      // A failed wait here surfaces at the next tile's barrier (or the ODone wait).
+      ok = free_p;
     }
     if (ok && n_my > 0) {
       ok = mbar_wait(BAR(kBarODone), 0, abort_flag, p.status);
@@ -353,9 +394,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
     const float l_row = l + xch[(wg ^ 1) * 128 + t];
     const bool have = ok && n_my > 0;
-    __half* orow = p.o + static_cast<long long>(b) * p.o_batch + static_cast<long long>(row) * p.o_tok +
-                   static_cast<long long>(h - p.o_head_base) * p.o_head;
+    const int st_id = threadIdx.x;  // 0..255 over both softmax warpgroups
+    const int oh = h - p.o_head_base;
     if (ns == 1) {
+      // Normalise and stage O as fp16 in the tensor-store box layout (HD/64
+      // panels of 128 rows x 128 B, 128-byte swizzle) over the idle Q region,
+      // then one thread stores it with TMA (rows past q_len are clipped).
       if (have) {
         const float inv_l = 1.f / l_row;
 #pragma unroll 1
@@ -363,90 +407,112 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t o[32];
           tmem_ld32(o_addr + c4 * 32, o);
           tmem_ld_wait(o);
-          if (row < p.q_len) {
-            __half* dst = orow + wg * (HD / 2) + c4 * 32;
+          const int col = wg * (HD / 2) + c4 * 32;
+          const uint32_t prow = base + (col >> 6) * 16384 + t * 128;
+          const int u0 = (col & 63) >> 3;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l);
-              v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
-              v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
-              v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(dst + i * 8) = v;
-            }
-          }
+          for (int i = 0; i < 4; ++i)
+            st_shared_v4(prow + (((u0 + i) ^ (t & 7)) << 4),
+                         pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l),
+                         pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l),
+                         pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l),
+                         pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l));
         }
       }
+      fence_proxy_async_smem();
+      named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
+      if (st_id == 0 && have) {
+        for (int pnl = 0; pnl < HD / 64; ++pnl)
+          for (int r32 = 0; r32 < 4 && q0 + 32 * r32 < p.q_len; ++r32)
+            tma_store_4d(&tm_o, base + pnl * 16384 + r32 * 4096, 64 * pnl, q0 + 32 * r32, oh, b);
+        tma_store_commit();
+        tma_store_wait_all();
+      }
     } else {
-      // Cluster merge; the producer and MMA warps take the same three cluster
-      // barriers below.
+      // Cluster merge by rows: rank r finishes rows [R*r, R*r + R) of the tile,
+      // R = 128 / n_split.  Each CTA sends the raw O and (m, l) of those rows to
+      // rank r; a warp's lanes are consecutive rows, so in the quad-major
+      // receive layout [sender][column quad][row][4] every remote store
+      // instruction writes 512 contiguous bytes.  The producer and MMA warps
+      // take the same two cluster barriers below.
+      const int R = 128 / ns;
+      const uint32_t sRecv = base;
+      const uint32_t sStats = base + 128u * HD * 4;   // [sender][row] (m, l)
+      const uint32_t sStage = sStats + 1024;          // 32 rows x HD fp16, store box layout
       fence_proxy_async_smem();
       cluster_sync();  // 1: every CTA's copies and MMAs are done: its ring may be overwritten
-      const uint32_t sStats = base + L::kStats;
-      if (wg == 0) {
-        const float mo = have ? m : -INFINITY, lo = have ? l_row : 0.f;
-        for (int r = 0; r < ns; ++r)
-          st_cluster_v2f(mapa_shared(sStats + (rank * 128 + t) * 8, r), mo, lo);
-      }
-      cluster_sync();  // 2: statistics of every split are in place
-      float M = -INFINITY;
-      for (int r = 0; r < ns; ++r) {
-        const float2 ml = ld_shared_v2f(sStats + (r * 128 + t) * 8);
-        if (ml.y > 0.f) M = fmaxf(M, ml.x);
-      }
-      float Lsum = 0.f;
-      for (int r = 0; r < ns; ++r) {
-        const float2 ml = ld_shared_v2f(sStats + (r * 128 + t) * 8);
-        if (ml.y > 0.f) Lsum += ml.y * ex2_approx(ml.x - M);
-      }
-      const float f = (have && l_row > 0.f) ? ex2_approx(m - M) / Lsum : 0.f;
-      const int W = HD / ns;  // output columns each rank finishes
+      const int owner = t / R, r_loc = t % R;
+      if (wg == 0)
+        st_cluster_v2f(mapa_shared(sStats + (rank * R + r_loc) * 8, owner), have ? m : -INFINITY,
+                       have ? l_row : 0.f);
 #pragma unroll 1
       for (int c4 = 0; c4 < HD / 64; ++c4) {
         uint32_t o[32];
         if (have) {
           tmem_ld32(o_addr + c4 * 32, o);
           tmem_ld_wait(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        const int col = wg * (HD / 2) + c4 * 32;  // 32 columns, all owned by one rank (W % 32 == 0)
-        const int owner = col / W;
-        const uint32_t dst = mapa_shared(
-            base + static_cast<uint32_t>(((rank * 128 + t) * (W + 4) + (col - owner * W)) * 4), owner);
+        const int cq0 = (wg * (HD / 2) + c4 * 32) >> 2;
+        const uint32_t dst = mapa_shared(sRecv + ((rank * (HD / 4) + cq0) * R + r_loc) * 16, owner);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_cluster_v4(dst + i * 16, o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          st_cluster_v4(dst + i * R * 16, o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
       }
-      cluster_sync();  // 3: every slice has arrived
-      if (row < p.q_len) {
-        const int half_w = W / 2;  // columns per thread: a multiple of 16 for ns 2, 4
-        __half* dst = orow + rank * W + wg * half_w;
-#pragma unroll 1
-        for (int c8 = 0; c8 < half_w; c8 += 8) {
-          float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-          for (int r = 0; r < ns; ++r) {
-            const uint32_t src = base + static_cast<uint32_t>(((r * 128 + t) * (W + 4) + wg * half_w + c8) * 4);
-            const float4 x0 = ld_shared_v4f(src), x1 = ld_shared_v4f(src + 16);
-            a0.x += x0.x; a0.y += x0.y; a0.z += x0.z; a0.w += x0.w;
-            a1.x += x1.x; a1.y += x1.y; a1.z += x1.z; a1.w += x1.w;
+      cluster_sync();  // 2: every sender's rows have arrived
+      // out = sum_s O_s * 2^(m_s - M) / L, M = max_s m_s, L = sum_s l_s 2^(m_s - M);
+      // 32 rows per round, staged as fp16 and stored with TMA.
+      for (int r0 = 0; r0 < R; r0 += 32) {
+        const int r = r0 + (st_id & 31);  // this thread's row in every pass of the round
+        float wgt[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          float M = -INFINITY, Lsum = 0.f;
+          for (int sdr = 0; sdr < ns; ++sdr) {
+            const float2 ml = ld_shared_v2f(sStats + (sdr * R + r) * 8);
+            if (ml.y > 0.f) M = fmaxf(M, ml.x);
           }
-          uint4 v;
-          v.x = pack_half2(a0.x, a0.y);
-          v.y = pack_half2(a0.z, a0.w);
-          v.z = pack_half2(a1.x, a1.y);
-          v.w = pack_half2(a1.z, a1.w);
-          *reinterpret_cast<uint4*>(dst + c8) = v;
+          for (int sdr = 0; sdr < ns; ++sdr) {
+            const float2 ml = ld_shared_v2f(sStats + (sdr * R + r) * 8);
+            if (ml.y > 0.f) {
+              wgt[sdr] = ex2_approx(ml.x - M);
+              Lsum += ml.y * wgt[sdr];
+            }
+          }
+          const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+          for (int sdr = 0; sdr < ns; ++sdr) wgt[sdr] *= inv;
         }
+        const int rr = st_id & 31;
+#pragma unroll 1
+        for (int cq = st_id >> 5; cq < HD / 4; cq += kSoftmaxThreads / 32) {
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sdr = 0; sdr < ns; ++sdr) {
+            const float4 x = ld_shared_v4f(sRecv + ((sdr * (HD / 4) + cq) * R + r) * 16);
+            a.x += wgt[sdr] * x.x;
+            a.y += wgt[sdr] * x.y;
+            a.z += wgt[sdr] * x.z;
+            a.w += wgt[sdr] * x.w;
+          }
+          const uint32_t unit = static_cast<uint32_t>(((cq & 15) >> 1) ^ (rr & 7));
+          st_shared_v2(sStage + (cq >> 4) * 4096 + rr * 128 + (unit << 4) + (cq & 1) * 8,
+                       pack_half2(a.x, a.y), pack_half2(a.z, a.w));
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
+        const int row0 = q0 + rank * R + r0;
+        if (st_id == 0 && row0 < p.q_len) {
+          for (int pnl = 0; pnl < HD / 64; ++pnl)
+            tma_store_4d(&tm_o, sStage + pnl * 4096, 64 * pnl, row0, oh, b);
+          tma_store_commit();
+          tma_store_wait_all();
+        }
+        named_bar_sync(kSoftmaxBar, kSoftmaxThreads);  // the stage may be refilled
       }
     }
   }
   if (ns > 1 && warp >= 8) {
     fence_proxy_async_smem();
-    cluster_sync();
     cluster_sync();
     cluster_sync();
   }
@@ -534,7 +600,12 @@ cudaError_t launch_wide_hd(const CUtensorMap& tq, const CUtensorMap& tk, const C
     cfg.attrs = nullptr;
     cfg.numAttrs = 0;
   }
-  e = cudaLaunchKernelEx(&cfg, attn_wide_sm100_kernel<HD>, tq, tk, tv, q);
+  // Output view [batch][heads][q_len][HD] for the tensor stores (box 64 x 32).
+  CUtensorMap to;
+  if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
+                   p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
+    return cudaErrorInvalidValue;
+  e = cudaLaunchKernelEx(&cfg, attn_wide_sm100_kernel<HD>, tq, tk, tv, to, q);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -116,6 +116,23 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 4-D tiled tensor store from shared memory (bulk-group completion); elements
+// outside the tensor's extents are not written.
+__device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(tmap),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed store group has completed (its global writes done).
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -366,6 +383,9 @@ __device__ __forceinline__ float4 ld_shared_v4f(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
+}
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
 }
 __device__ __forceinline__ float2 ld_shared_v2f(uint32_t addr) {
   float2 v;
