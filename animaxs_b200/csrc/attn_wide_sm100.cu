@@ -32,11 +32,17 @@
 // each tile's keys over a thread-block cluster of n_split (2 or 4) CTAs; each
 // computes an unnormalised partial O with its own row max m and sum l, and the
 // cluster merges them through distributed shared memory, with no global
-// workspace: every CTA sends (m, l) per row to all CTAs, scales its O by
-// 2^(m - M) / L (M, L the merged max and sum) and sends column slice r of the
-// result to CTA r, which adds the n_split slices and stores its HD/n_split
-// output columns.  The receive buffers overlay the Q/K/V ring, which is idle by
-// then (the first cluster barrier follows every CTA's last MMA and copy).
+// workspace: the CTA of split s finishes rows [R*s, R*s + R), R = 128 /
+// n_split; every CTA sends those rows' raw O and (m, l) to it, and it stores
+// sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M) (M = max_s m_s).  The receive
+// buffers overlay the Q/P/ring region, idle once every CTA's MMAs and copies
+// are done (the first cluster barrier).
+//
+// Measured on B200 and not kept: the same kernel as a tcgen05 CTA pair
+// (cta_group::2, M = 256, each CTA loading half of every K/V chunk) halves the
+// MMA instructions, but with a single S buffer the pair waits on the slower
+// of two softmaxes plus the cross-SM signal latency every tile, and ran
+// 10% (one image: 2x, clusters of 8) slower.
 #include <atomic>
 
 #include "api_internal.h"

@@ -413,6 +413,146 @@ def run_cfg5(args, rank, world, local_rank):
         "clocks": clocks}), flush=True)
 
 
+VAE_POS = 64 * 64
+VAE_CH = 384
+VAE_FLOPS = 4.0 * VAE_POS * VAE_POS * VAE_CH       # 25.8 GFLOP per image
+VAE_POOL = 16                                      # 16 x 9.4 MiB of split QKV (> 126 MB L2)
+
+
+def run_vae(args, rank, world, local_rank):
+    """The VAE decoder's middle attention (VAEDecoder.swift:351-410): one head
+    of 384 channels over the 64x64 latent positions, one image per call, in the
+    reference's call form (AttentionExecutor.encode on a split [3 x positions,
+    384] QKV buffer with byte offsets, head-major).  Images are independent:
+    each rank decodes its own (weak scaling).  value = images/s over all ranks;
+    inputs rotate through a pool larger than L2."""
+    import torch
+    import torch.distributed as dist
+
+    import animaxs_b200 as ax
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ex = ax.AttentionExecutor(local_rank)
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(4321 + rank)
+    pool = [torch.randn(3 * VAE_POS, VAE_CH, generator=g, device=device).half() for _ in range(VAE_POOL)]
+    out = torch.empty(VAE_POS, VAE_CH, dtype=torch.float16, device=device)
+    kw = dict(heads=1, query_count=VAE_POS, key_count=VAE_POS, head_dim=VAE_CH,
+              key_offset=VAE_POS * VAE_CH * 2, value_offset=2 * VAE_POS * VAE_CH * 2)
+
+    # The timed loop calls the same C-ABI forward through the cached strided
+    # descriptor ([1, positions, 1, 384] views of the split buffer: the same
+    # descriptor contents as the head-major encode call, without rebuilding it
+    # on the host every call); the e2e leg below uses encode itself.
+    views = [tuple(x[j * VAE_POS:(j + 1) * VAE_POS].view(1, VAE_POS, 1, VAE_CH) for j in range(3))
+             for x in pool]
+    out_v = out.view(1, VAE_POS, 1, VAE_CH)
+
+    def call(i):
+        q, k, v = views[i % VAE_POOL]
+        ex.attention(q, k, v, out=out_v, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    calls_per_step = 4096  # ~0.16 s per step: long enough for the clock sampler
+    for i in range(args.warmup * calls_per_step):
+        call(i)
+    barrier()
+    ex.synchronize(stream)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    ex.set_kernel_timing(True)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps * calls_per_step):
+        call(i)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ex.set_kernel_timing(False)
+    n_kern, kern_total_ms, kern_max_ms = ex.kernel_timing()
+    ex.synchronize(stream)
+    el = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([el], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    images = args.steps * calls_per_step * world
+
+    e2e = None
+    if not args.no_e2e:
+        # Pinned host split-QKV in, output back to the host, every image.
+        hg = torch.Generator().manual_seed(77)
+        host = [torch.randn(3 * VAE_POS, VAE_CH, generator=hg).half().pin_memory() for _ in range(4)]
+        host_out = torch.empty(VAE_POS, VAE_CH, dtype=torch.float16).pin_memory()
+        dev_in = torch.empty(3 * VAE_POS, VAE_CH, dtype=torch.float16, device=device)
+        n_e2e = max(16, args.steps * 8)
+        for i in range(4):
+            dev_in.copy_(host[i], non_blocking=True)
+            ex.encode(stream, dev_in, dev_in, dev_in, out, **kw)
+            host_out.copy_(out, non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n_e2e):
+            dev_in.copy_(host[i % 4], non_blocking=True)
+            ex.encode(stream, dev_in, dev_in, dev_in, out, **kw)
+            host_out.copy_(out, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        ee = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ee], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ee = float(t.item())
+        e2e = {"value": n_e2e * world / (ee / 1e3), "unit": "img/s",
+               "h2d_bytes_per_step": 3 * VAE_POS * VAE_CH * 2, "d2h_bytes_per_step": VAE_POS * VAE_CH * 2,
+               "steps": n_e2e, "path": "AttentionExecutor.encode -> animaxs_attn_forward (host QKV in, output out)"}
+    if rank != 0:
+        return
+    peak_burst, peak_sust, _, peak_kind = peaks()
+    avg_kern = kern_total_ms / n_kern if n_kern else float("nan")
+    achieved = VAE_FLOPS / (avg_kern / 1e3) / 1e12
+    line = {
+        "metric": "VAE middle attention throughput (1 head x 384 over the 64x64 latent, one image per call)",
+        "value": images / (el / 1e3), "unit": "img/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": f"vae: {calls_per_step} images per step, 4096 positions x 384, heads 1, "
+                               "split QKV buffer with byte offsets (the reference's call)",
+                   "parallelism": f"images x{world}",
+                   "l2": f"inputs cycled over a {VAE_POOL * 9} MiB resident pool (> 126 MB L2)"},
+        "roofline": {"kernel": "attn_wide_sm100_kernel<384> (4096 x 4096 x 384, keys split over a cluster)",
+                     "bound": "tensor", "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                     "frac": achieved / peak_sust, "peak_kind": f"{peak_kind} bf16 dense, sustained",
+                     "frac_of_burst_peak": achieved / peak_burst, "flops_per_launch": VAE_FLOPS,
+                     "avg_launch_ms": avg_kern, "max_launch_ms": kern_max_ms, "launches_timed": n_kern,
+                     "traffic": None, "algorithmic_bytes": 4 * VAE_POS * VAE_CH * 2},
+        "clocks": clocks,
+        "gpu_launches": args.steps * calls_per_step,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import attn_oracle as ora  # the checker, used here only as the CPU baseline
+        import numpy as np
+        qkv = pool[0].float().cpu().numpy().reshape(3, 1, VAE_POS, 1, VAE_CH)
+        rows = np.arange(512)
+        t_c = time.perf_counter()
+        ora.attention(qkv[0], qkv[1], qkv[2], rows=rows)
+        t_c = time.perf_counter() - t_c
+        line["cpu_baseline"] = {"value": 1.0 / (t_c * VAE_POS / len(rows)), "unit": "img/s",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": "512 of 4096 query rows of one image, numpy fp32 oracle, x8"}
+    print(json.dumps(line), flush=True)
+
+
 def profile_kernel(args):
     import torch
 
@@ -438,9 +578,10 @@ def main():
     ap.add_argument("--impl", default="animaxs", choices=["animaxs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5"],
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae"],
                     help="cfg4 (default): the 8-step DiT workload, batch-sharded; cfg5: the "
-                         "16384-token self-attention, heads sharded + one NCCL all-gather")
+                         "16384-token self-attention, heads sharded + one NCCL all-gather; vae: "
+                         "the VAE decoder's middle attention (one head of 384), images per rank")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only run the fused rms+rope3d self-attention (prologue + flash kernel) "
                          "on a batch-4 4096-token case (192 MiB of inputs, > L2): the small "
@@ -466,6 +607,8 @@ def main():
     try:
         if args.workload == "cfg5":
             run_cfg5(args, rank, world, local_rank)
+        elif args.workload == "vae":
+            run_vae(args, rank, world, local_rank)
         else:
             run_gpu(args, rank, world, local_rank)
     finally:
