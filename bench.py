@@ -558,6 +558,20 @@ def profile_kernel(args):
 
     import animaxs_b200 as ax
     ex = ax.AttentionExecutor(0)
+    if args.workload == "vae":
+        # warmup + steps VAE middle-attention calls on distinct images (> L2 in total)
+        g = torch.Generator(device="cuda").manual_seed(5)
+        pool = [torch.randn(3 * VAE_POS, VAE_CH, generator=g, device="cuda").half() for _ in range(VAE_POOL)]
+        out = torch.empty(VAE_POS, VAE_CH, dtype=torch.float16, device="cuda")
+        stream = torch.cuda.current_stream()
+        for i in range(args.warmup + args.steps):
+            qkv = pool[i % VAE_POOL]
+            ex.encode(stream, qkv, qkv, qkv, out, heads=1, query_count=VAE_POS, key_count=VAE_POS,
+                      head_dim=VAE_CH, key_offset=VAE_POS * VAE_CH * 2, value_offset=2 * VAE_POS * VAE_CH * 2)
+        torch.cuda.synchronize()
+        ex.synchronize()
+        print("profile-kernel done", flush=True)
+        return
     g = torch.Generator(device="cuda").manual_seed(5)
     shape = (4, S_SELF, HEADS, HD)
     q, k, v = (torch.randn(*shape, generator=g, device="cuda").half() for _ in range(3))
@@ -584,8 +598,9 @@ def main():
                          "the VAE decoder's middle attention (one head of 384), images per rank")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only run the fused rms+rope3d self-attention (prologue + flash kernel) "
-                         "on a batch-4 4096-token case (192 MiB of inputs, > L2): the small "
-                         "case for ncu captures")
+                         "on a batch-4 4096-token case (192 MiB of inputs, > L2), or with "
+                         "--workload vae warmup+steps VAE middle-attention calls: the small "
+                         "cases for ncu captures")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
