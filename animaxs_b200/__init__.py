@@ -3,10 +3,12 @@
 The product is ``libanimaxs_attn.so`` (C ABI, ``include/animaxs_attn.h``); this
 package holds its CUDA sources (``csrc/``), the in-tree build
 (``build.py``) and the host-side mirror of the reference's Swift
-``AttentionExecutor`` interface (``executor.py``).
+``AttentionExecutor`` interface (``executor.py``), plus the fused attention
+projections (``projection.py``).
 """
 
 from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError,  # noqa: F401
                    AttentionValidationError, LIB_PATH, lib)
 from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  # noqa: F401
                        DitRoPE, GqaHeadMapping, adapter_rope, qwen_rope)
+from .projection import ProjectionExecutor  # noqa: F401,E402

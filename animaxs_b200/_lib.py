@@ -73,6 +73,20 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class ProjDesc(ctypes.Structure):
+    _fields_ = [
+        ("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+        ("x_stride", ctypes.c_int64), ("w_stride", ctypes.c_int64), ("out_stride", ctypes.c_int64),
+        ("epilogue", ctypes.c_int32), ("tokens", ctypes.c_int32), ("qk_norm", ctypes.c_int32),
+        ("q_cols", ctypes.c_int32), ("k_cols", ctypes.c_int32), ("rope_rows", ctypes.c_int32),
+        ("q_norm_weight", ctypes.c_void_p), ("k_norm_weight", ctypes.c_void_p),
+        ("rope_table", ctypes.c_void_p), ("eps", ctypes.c_float), ("reserved0", ctypes.c_int32),
+        ("gate", ctypes.c_void_p), ("gate_stride", ctypes.c_int64),
+    ]
+
+
+PROJ_STORE, PROJ_QKV_NORM, PROJ_GATE_ADD = 0, 1, 2
+
 # name -> (restype, argtypes); every symbol the header declares.
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -102,6 +116,9 @@ SIGNATURES = {
     "animaxs_comm_destroy": (_I, [_P]),
     "animaxs_attn_forward_head_sharded": (_I, [_P, _P, _DESC, _P, _P, _P, _P, _P]),
     "animaxs_attn_forward_noalloc": (_I, [_DESC, _P, _P, _P, _P, _P]),
+    "animaxs_proj_desc_init": (_I, [ctypes.POINTER(ProjDesc), _I, _I, _I, _I]),
+    "animaxs_proj_validate": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P]),
+    "animaxs_proj_forward": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libanimaxs_attn.so")
 SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "attn_wide_sm100.cu", "qk_norm.cu", "sharded.cu",
-           "noalloc.cu"]
+           "noalloc.cu", "proj_api.cu", "proj_sm100.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
          "--expt-relaxed-constexpr", "-Xptxas", "-v"]
@@ -45,27 +45,37 @@ def _headers():
     return hs
 
 
+# Kernels that re-split their registers with setmaxnreg: source file ->
+# (kernel-name pattern in the ptxas report, raised-count define, lowered-count
+# define, raised-thread-count constant).
+REGISTER_SPLITS = {
+    "attn_fwd_sm100.cu": ("attn_fwd_sm100_kernel", "AX_SOFTMAX_REGS", "AX_OTHER_REGS", "kSoftmaxThreads"),
+    "proj_sm100.cu": ("proj_sm100_kernel", "AX_EPI_REGS", "AX_PROJ_OTHER_REGS", "kEpiThreads"),
+}
+
+
 def check_register_split(source: str, ptxas_log: str) -> None:
-    """The flash kernel re-splits its registers with setmaxnreg; the raise waits
-    until enough registers are free in the CTA's launch allocation, so the new
-    shares must fit into (threads x registers ptxas gave each thread at launch).
-    Refuse to build otherwise."""
+    """A kernel that re-splits its registers with setmaxnreg raises some
+    warpgroups' counts; the raise waits until enough registers are free in the
+    CTA's launch allocation, so the new shares must fit into (threads x
+    registers ptxas gave each thread at launch).  Refuse to build otherwise."""
     import re
+    kernel, hi_def, lo_def, hi_threads = REGISTER_SPLITS[os.path.basename(source)]
     text = open(source).read()
-    soft = int(re.search(r"#define AX_SOFTMAX_REGS (\d+)", text).group(1))
-    other = int(re.search(r"#define AX_OTHER_REGS (\d+)", text).group(1))
+    soft = int(re.search(rf"#define {hi_def} (\d+)", text).group(1))
+    other = int(re.search(rf"#define {lo_def} (\d+)", text).group(1))
     threads = int(re.search(r"constexpr int kThreads = (\d+);", text).group(1))
-    ms = re.search(r"constexpr int kSoftmaxThreads = (\d+);", text)
+    ms = re.search(rf"constexpr int {hi_threads} = (\d+);", text)
     softmax_threads = int(ms.group(1)) if ms else 256
-    counts = re.findall(r"entry function '[^']*attn_fwd_sm100_kernel[^']*'.*?Used (\d+) registers",
-                        ptxas_log, re.S)
+    counts = re.findall(rf"entry function '[^']*{kernel}[^']*'.*?Used (\d+) registers", ptxas_log, re.S)
     if not counts:
-        raise RuntimeError("could not read the flash kernel's register count from ptxas")
+        raise RuntimeError(f"could not read {kernel}'s register count from ptxas")
     need = softmax_threads * soft + (threads - softmax_threads) * other
-    for launch in map(int, counts):  # one per head-dim instantiation
+    for launch in map(int, counts):  # one per template instantiation
         if need > threads * launch or soft % 8 or other % 8:
-            raise RuntimeError(f"register split {softmax_threads}x{soft} + {threads - softmax_threads}x{other} "
-                               f"= {need} exceeds the launch allocation {threads}x{launch} = {threads * launch}")
+            raise RuntimeError(f"{kernel}: register split {softmax_threads}x{soft} + "
+                               f"{threads - softmax_threads}x{other} = {need} exceeds the launch "
+                               f"allocation {threads}x{launch} = {threads * launch}")
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -90,7 +100,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         for cmd, res in logs:
             sys.stderr.write(f"--- {os.path.basename(cmd[-3])}\n{res.stderr}")
     for cmd, res in logs:
-        if cmd[-3].endswith("attn_fwd_sm100.cu"):
+        if os.path.basename(cmd[-3]) in REGISTER_SPLITS:
             check_register_split(cmd[-3], res.stderr)
     if force or jobs or not _newer(LIB, objs):
         link = [cc, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-ldl", "-Xcompiler", "-fPIC"]

@@ -35,6 +35,7 @@ struct AxOutView {
 
 int ax_set_error(animaxs_attn_ctx* ctx, int code, const char* fmt, ...);
 int ax_cuda_fail(animaxs_attn_ctx* ctx, cudaError_t e, const char* what);
+int ax_ensure_scratch(animaxs_attn_ctx* ctx, size_t bytes);  // context scratch of at least `bytes`
 int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q, const void* k,
                 const void* v, const void* o);
 int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int64_t dim, int64_t rows,

@@ -71,4 +71,32 @@ int attn_fwd_rows_per_cta();  // query rows one attention CTA covers (head dims 
 
 cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
 
+// Fused attention projections (proj_sm100.cu): out = x w^T over fp16 operands
+// with fp32 accumulation, then one of three epilogues.
+enum ProjMode : int {
+  kProjStore = 0,    // out fp16 = fp16(acc)
+  kProjQkvNorm = 1,  // q / k column ranges: per-128-column-head RMSNorm (+ split-half RoPE)
+  kProjGateAdd = 2,  // residual fp32 += float(fp16(acc)) * gate[row / tokens][col]
+};
+struct ProjParams {
+  int m, n, k;
+  int tokens;               // rows per image (RoPE row = row % tokens, gate row = row / tokens)
+  int mode;                 // ProjMode
+  int q_cols, k_cols;       // kProjQkvNorm: [0, q_cols) q heads, [q_cols, q_cols + k_cols) k heads
+  const __half* q_w;        // kProjQkvNorm: shared [128] norm weights, or nullptr (ones)
+  const __half* k_w;
+  const float* rope;        // pair-major [64][tokens] (cos, sin) float2 (launch_rope_pairs), or nullptr
+  float eps;
+  const float* gate;        // kProjGateAdd: [images][gate_stride] fp32
+  long long gate_stride;
+  int tiles_n;              // ceil(n / 256)
+  int tiles;                // ceil(m / 128) * tiles_n
+  unsigned int* status;
+};
+cudaError_t launch_proj(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tout,
+                        const ProjParams& p, cudaStream_t stream);
+int proj_kernel_attributes(int* regs, int* max_threads, int* smem_static, int* smem_dynamic_max);
+// [rows][64][2][2] table blocks -> [64][rows] (cos, sin) pairs in `out` (rows*512 bytes).
+cudaError_t launch_rope_pairs(const float* table, void* out, int rows, cudaStream_t stream);
+
 }  // namespace ax

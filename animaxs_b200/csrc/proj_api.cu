@@ -1,0 +1,185 @@
+// proj_api.cu -- C ABI of the fused attention projections (include/animaxs_attn.h):
+// validation, 2-D tensor maps, launch.  The kernel is proj_sm100.cu.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/animaxs_attn.h"
+#include "api_internal.h"
+#include "kernels.h"
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [rows][cols] row-major matrix with `stride` elements between rows; box
+// box_cols x box_rows, 128-byte swizzle (box_cols * element size == 128).
+int make_tmap_2d(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, bool f32, int64_t cols,
+                 int64_t rows, int64_t stride, int box_cols, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr)
+    return ax_set_error(ctx, ANIMAXS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const int64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(rows > 1 ? stride * es : cols * es + (16 - cols * es % 16) % 16)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return ax_set_error(ctx, ANIMAXS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return ANIMAXS_OK;
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+int proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void* x, const void* w,
+                  const void* out) {
+  if (d == nullptr) return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "null descriptor");
+  if (x == nullptr || w == nullptr || out == nullptr)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "projection buffers must not be null");
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0 || d->tokens <= 0)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "invalid projection shape");
+  if (d->epilogue < ANIMAXS_PROJ_STORE || d->epilogue > ANIMAXS_PROJ_GATE_ADD)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown projection epilogue %d", d->epilogue);
+  const bool f32_out = d->epilogue == ANIMAXS_PROJ_GATE_ADD;
+  if (d->k % 8 != 0 || d->x_stride < d->k || d->x_stride % 8 != 0 || d->w_stride < d->k ||
+      d->w_stride % 8 != 0 || d->out_stride < d->n || d->out_stride % (f32_out ? 4 : 8) != 0 ||
+      !aligned16(x) || !aligned16(w) || !aligned16(out))
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
+                        "projection requires 16-byte-aligned buffers and row strides, k a multiple of 8");
+  if (d->x_stride >= (int64_t{1} << 38) || d->w_stride >= (int64_t{1} << 38) ||
+      d->out_stride >= (int64_t{1} << 38))
+    return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "projection byte size overflow");
+  if (!(d->eps >= 0.f) || !std::isfinite(d->eps))
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "eps must be finite and >= 0");
+  if (d->epilogue == ANIMAXS_PROJ_QKV_NORM) {
+    if (d->qk_norm != ANIMAXS_QK_RMS && d->qk_norm != ANIMAXS_QK_RMS_ROPE)
+      return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "QKV_NORM needs qk_norm RMS or RMS_ROPE");
+    if (d->q_cols < 0 || d->k_cols < 0 || d->q_cols % 128 != 0 || d->k_cols % 128 != 0 ||
+        static_cast<int64_t>(d->q_cols) + d->k_cols > d->n || d->n % 128 != 0)
+      return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
+                          "QKV_NORM normalises heads of 128: q_cols, k_cols and n must be multiples of 128");
+    if (d->qk_norm == ANIMAXS_QK_RMS_ROPE &&
+        (d->rope_table == nullptr || d->rope_rows < d->tokens || !aligned16(d->rope_table)))
+      return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
+                          "RMS_ROPE needs a 16-byte-aligned rope table with >= tokens rows");
+    for (const void* wt : {d->q_norm_weight, d->k_norm_weight})
+      if (wt != nullptr && !aligned16(wt))
+        return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "norm weights must be 16-byte aligned");
+  }
+  if (d->epilogue == ANIMAXS_PROJ_GATE_ADD) {
+    if (d->gate == nullptr || d->gate_stride < d->n)
+      return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "GATE_ADD needs a gate with gate_stride >= n");
+  }
+  return ANIMAXS_OK;
+}
+
+}  // namespace
+
+extern "C" int animaxs_proj_desc_init(animaxs_proj_desc* d, int m, int n, int k, int epilogue) {
+  if (d == nullptr) return ANIMAXS_ERR_INVALID_ARG;
+  std::memset(d, 0, sizeof(*d));
+  d->m = m;
+  d->n = n;
+  d->k = k;
+  d->x_stride = k;
+  d->w_stride = k;
+  d->out_stride = n;
+  d->epilogue = epilogue;
+  d->tokens = m;
+  d->gate_stride = n;
+  d->eps = 1e-6f;
+  return ANIMAXS_OK;
+}
+
+extern "C" int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void* x,
+                                     const void* w, const void* out) {
+  const int rc = proj_validate(ctx, d, x, w, out);
+  if (rc == ANIMAXS_OK && ctx != nullptr) ctx->last_error.clear();
+  return rc;
+}
+
+extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void* x,
+                                    const void* w, void* out, void* stream) {
+  if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
+  int rc = proj_validate(ctx, d, x, w, out);
+  if (rc != ANIMAXS_OK) return rc;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != ctx->device) cudaSetDevice(ctx->device);
+  struct Restore {
+    int dev, prev;
+    ~Restore() {
+      if (dev != prev) cudaSetDevice(prev);
+    }
+  } restore{ctx->device, prev};
+
+  const bool f32_out = d->epilogue == ANIMAXS_PROJ_GATE_ADD;
+  CUtensorMap ta, tb, tout;
+  rc = make_tmap_2d(ctx, &ta, x, false, d->k, d->m, d->x_stride, 64, 128);
+  if (rc == ANIMAXS_OK) rc = make_tmap_2d(ctx, &tb, w, false, d->k, d->n, d->w_stride, 64, 256);
+  if (rc == ANIMAXS_OK)
+    rc = f32_out ? make_tmap_2d(ctx, &tout, out, true, d->n, d->m, d->out_stride, 32, 128)
+                 : make_tmap_2d(ctx, &tout, out, false, d->n, d->m, d->out_stride, 64, 128);
+  if (rc != ANIMAXS_OK) return rc;
+
+  ax::ProjParams p{};
+  p.m = d->m;
+  p.n = d->n;
+  p.k = d->k;
+  p.tokens = d->tokens;
+  p.mode = d->epilogue == ANIMAXS_PROJ_QKV_NORM ? ax::kProjQkvNorm
+           : f32_out                            ? ax::kProjGateAdd
+                                                : ax::kProjStore;
+  p.q_cols = d->q_cols;
+  p.k_cols = d->k_cols;
+  p.q_w = static_cast<const __half*>(d->q_norm_weight);
+  p.k_w = static_cast<const __half*>(d->k_norm_weight);
+  p.rope = nullptr;
+  if (d->epilogue == ANIMAXS_PROJ_QKV_NORM && d->qk_norm == ANIMAXS_QK_RMS_ROPE) {
+    // The epilogue reads the table pair-major: re-lay the `tokens` rows it uses
+    // out into context scratch (ordered before the GEMM on the same stream).
+    rc = ax_ensure_scratch(ctx, static_cast<size_t>(d->tokens) * 64 * 8);
+    if (rc != ANIMAXS_OK) return rc;
+    cudaError_t e = ax::launch_rope_pairs(d->rope_table, ctx->scratch, d->tokens, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "rope table re-layout");
+    p.rope = static_cast<const float*>(ctx->scratch);
+  }
+  p.eps = d->eps > 0.f ? d->eps : 1e-6f;
+  p.gate = d->gate;
+  p.gate_stride = d->gate_stride;
+  p.tiles_n = (d->n + 255) / 256;
+  const long long tiles = static_cast<long long>((d->m + 127) / 128) * p.tiles_n;
+  if (tiles > 0x7fffffffLL) return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "projection too large");
+  p.tiles = static_cast<int>(tiles);
+  p.status = ctx->d_status;
+  cudaError_t e = ax::launch_proj(ta, tb, tout, p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    int regs = 0, threads = 0, ss = 0, sd = 0;
+    ax::proj_kernel_attributes(&regs, &threads, &ss, &sd);
+    return ax_set_error(ctx, ANIMAXS_ERR_CUDA,
+                        "projection launch: %s (kernel: %d registers, max %d threads, %d B static + %d B "
+                        "dynamic shared memory allowed)",
+                        cudaGetErrorString(e), regs, threads, ss, sd);
+  }
+  ctx->last_error.clear();
+  return ANIMAXS_OK;
+}

@@ -241,6 +241,56 @@ int animaxs_gqa_kv_head(int query_head, int heads, int kv_heads);
 int animaxs_attn_forward_noalloc(const animaxs_attn_desc* desc, const void* q, const void* k,
                                  const void* v, void* o, void* stream);
 
+/* ---- Fused attention projections ------------------------------------------
+ * The GEMMs on either side of DiT attention, each with its elementwise step
+ * fused into the epilogue (one kernel per call).  The reference encodes them
+ * separately: LinearExecutor.encode (LinearExecutor.swift:79-) for q, k, v
+ * (DiTBlockExecutor.swift:1097-1131), then rms_rope_split_half /
+ * rmsnorm_heads_half on q and k (AnimaKernels.metal:660-729); after attention
+ * the out-projection and gate_add_half_f32 (DiTBlockExecutor.swift:1223-1236,
+ * AnimaKernels.metal:624-634).  x [m][k] and w [n][k] are fp16 (w is the
+ * reference's [out][in] weight); accumulation is fp32 and the projection is
+ * rounded to fp16 before any epilogue math, as the reference's fp16 output. */
+typedef enum animaxs_proj_epilogue {
+  ANIMAXS_PROJ_STORE = 0,    /* out fp16 [m][out_stride] = fp16(x w^T) */
+  ANIMAXS_PROJ_QKV_NORM = 1, /* as STORE; q and k heads then RMS-normalised (+ RoPE), v stored as is:
+                                a fused q|k|v projection ready for animaxs_attn_forward with
+                                qk_norm = NONE (strided views of `out`) */
+  ANIMAXS_PROJ_GATE_ADD = 2  /* residual fp32 [m][out_stride] += float(fp16(x w^T)) * gate[row/tokens][col]
+                                (gate_add_half_f32; `out` is the residual) */
+} animaxs_proj_epilogue;
+
+typedef struct animaxs_proj_desc {
+  int32_t m;                 /* rows = images x tokens (`inputRows:`) */
+  int32_t n;                 /* output features (rows of w) */
+  int32_t k;                 /* input features, a multiple of 8 */
+  int64_t x_stride;          /* elements between rows of x (>= k, multiple of 8) */
+  int64_t w_stride;          /* elements between rows of w (>= k, multiple of 8) */
+  int64_t out_stride;        /* elements between rows of out (>= n; multiple of 8 fp16 / 4 fp32) */
+  int32_t epilogue;          /* animaxs_proj_epilogue */
+  int32_t tokens;            /* rows per image: RoPE row = row % tokens, gate row = row / tokens */
+  int32_t qk_norm;           /* QKV_NORM: ANIMAXS_QK_RMS or ANIMAXS_QK_RMS_ROPE */
+  int32_t q_cols;            /* QKV_NORM: columns [0, q_cols) are q heads of 128 */
+  int32_t k_cols;            /* QKV_NORM: columns [q_cols, q_cols + k_cols) are k heads of 128 */
+  int32_t rope_rows;         /* rows of rope_table (>= tokens) */
+  const void* q_norm_weight; /* DEVICE fp16[128] shared by all q heads, or NULL for ones */
+  const void* k_norm_weight; /* DEVICE fp16[128], or NULL for ones */
+  const float* rope_table;   /* DEVICE fp32[rope_rows][64][2][2] blocks [cos,-sin,sin,cos] */
+  float eps;                 /* RMSNorm epsilon; 0 means 1e-6 */
+  int32_t reserved0;
+  const float* gate;         /* GATE_ADD: DEVICE fp32 [m / tokens][gate_stride] */
+  int64_t gate_stride;       /* elements between images' gate rows (>= n) */
+} animaxs_proj_desc;
+
+/* Dense defaults: strides = k / k / n, tokens = m, eps 1e-6. */
+int animaxs_proj_desc_init(animaxs_proj_desc* desc, int m, int n, int k, int epilogue);
+/* Validate exactly as animaxs_proj_forward does, without a GPU. */
+int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, const void* x,
+                          const void* w, const void* out);
+/* Enqueue the fused projection on `stream`. */
+int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, const void* x,
+                         const void* w, void* out, void* stream);
+
 /* ---- Multi-GPU: heads sharded across ranks + one NCCL all-gather ----------
  * No counterpart exists in the reference (a single-device app); this serves
  * the 16K-token DiT configuration.  NCCL is loaded at run time (dlopen of

@@ -257,3 +257,55 @@ def parity(actual_fp16: np.ndarray, oracle_fp32: np.ndarray) -> tuple[float, flo
     e = to_fp16_storage(oracle_fp32)
     diff = np.abs(a - e)
     return float(diff.max()), float(diff.mean())
+
+
+# ---------------------------------------------------------------------------
+# The projections on either side of attention (fused epilogues)
+# ---------------------------------------------------------------------------
+def linear_fp16(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """``x @ w^T`` with fp32 accumulation, rounded to fp16 (returned as fp32).
+
+    dit_source_oracle.py:93-96 (``linear``: F.linear in fp32, cast to the input
+    dtype) -- the reference's LinearExecutor output (LinearExecutor.swift:79-)
+    is fp16.  ``x`` is ``[m, k]``, ``w`` the ``[n, k]`` (out, in) weight.
+    """
+    xf = np.asarray(x, dtype=np.float32)
+    wf = np.asarray(w, dtype=np.float32)
+    return to_fp16_storage(xf @ wf.T)
+
+
+def qkv_norm_projection(x, w, *, q_cols: int, k_cols: int, qk_norm: str = "rms_rope",
+                        q_norm_weight=None, k_norm_weight=None, rope_table=None,
+                        tokens: int | None = None, eps: float = EPS) -> np.ndarray:
+    """The fused q|k|v projection: ``y = linear_fp16(x, w)``; the q heads
+    (columns ``[0, q_cols)``) and k heads (``[q_cols, q_cols + k_cols)``), 128
+    wide, are RMS-normalised with fp32 statistics (``rms_norm_heads``) and, for
+    ``"rms_rope"``, rotated (``apply_split_half_rope``, table row = row % tokens);
+    the rest (v) is ``y``.  DiTBlockExecutor.swift:1097-1131 then
+    AnimaKernels.metal:660-729 (dit_source_oracle.py:262-272).  fp32 result,
+    to be compared after fp16 storage.
+    """
+    y = linear_fp16(x, w)
+    m = y.shape[0]
+    tokens = m if tokens is None else tokens
+    out = y.copy()
+    for c0, c1, wt in ((0, q_cols, q_norm_weight), (q_cols, q_cols + k_cols, k_norm_weight)):
+        if c1 <= c0:
+            continue
+        h = y[:, c0:c1].reshape(m // tokens, tokens, (c1 - c0) // 128, 128)
+        h = rms_norm_heads(h, wt, eps)
+        if qk_norm == "rms_rope":
+            h = apply_split_half_rope(h, rope_table)
+        out[:, c0:c1] = h.reshape(m, c1 - c0)
+    return out
+
+
+def gate_add_projection(residual, x, w, gate, *, tokens: int) -> np.ndarray:
+    """``residual + float(linear_fp16(x, w)) * gate[row // tokens]`` in fp32:
+    the out-projection then gate_add_half_f32 (AnimaKernels.metal:624-634,
+    DiTBlockExecutor.swift:1223-1236; dit_source_oracle.py:317
+    ``x + gate * out``)."""
+    branch = linear_fp16(x, w)
+    g = np.asarray(gate, dtype=np.float32)
+    rows = np.arange(branch.shape[0]) // tokens
+    return (np.asarray(residual, dtype=np.float32) + branch * g[rows]).astype(np.float32)

@@ -152,3 +152,31 @@ def workload_block(prompt: int, step: int, block: int):
                      rope_table=ora.dit_rope_table(1, 64, 64))
     cross_case = Case("wl_cross", cq, ck, cv, qk_norm="rms")
     return self_case, cross_case
+
+
+def proj_qkv(seed: int, images: int = 2, tokens: int = 64, k: int = 256, q_heads: int = 2,
+             k_heads: int = 2, v_cols: int = 256):
+    """Inputs of the fused q|k|v projection: x [images*tokens, k] ~ N(0, 1),
+    w [q_heads*128 + k_heads*128 + v_cols, k] ~ N(0, 1/k) (unit-variance
+    projections), norm weights ~ 1 + N(0, 0.1^2); fp16.  Drawn in that order."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    n = (q_heads + k_heads) * 128 + v_cols
+    x = torch.randn(images * tokens, k, generator=g).half().numpy()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half().numpy()
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).half().numpy()
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).half().numpy()
+    return x, w, qw, kw
+
+
+def proj_gate(seed: int, images: int = 2, tokens: int = 64, k: int = 256, n: int = 256):
+    """Inputs of the out-projection + gated residual: x [images*tokens, k] fp16,
+    w [n, k] ~ N(0, 1/k) fp16, residual [images*tokens, n] fp32, gate
+    [images, n] fp32 ~ N(0, 0.5^2).  Drawn in that order."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    x = torch.randn(images * tokens, k, generator=g).half().numpy()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half().numpy()
+    residual = torch.randn(images * tokens, n, generator=g).numpy()
+    gate = (0.5 * torch.randn(images, n, generator=g)).numpy()
+    return x, w, residual, gate

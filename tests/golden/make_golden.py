@@ -19,6 +19,9 @@ calls their functions -- ``rms_norm``, ``dit_rope``, ``apply_split_half_rope``,
   GQA prefill with causal + padding masks).
 * ``attn_configs.npz``  -- outputs at sampled query rows for the benchmark
   configurations 1, 2, 3 (layers 0 and 27), 4 (a subset of blocks) and 5.
+* ``proj_small.npz``    -- the fused projections (q|k|v with RMSNorm and
+  RoPE, and the out-projection's gated residual) through ``linear``,
+  ``rms_norm``, ``dit_rope`` and ``apply_split_half_rope``.
 
 Only the inputs' seeds are stored (plus checksums of the inputs to detect a
 change in ``torch.Generator``); tests regenerate inputs with
@@ -117,15 +120,51 @@ def ref_qwen(case, rows):
     return ref_masked(case, xq.transpose(1, 2), xk.transpose(1, 2), v, rows, causal=True)
 
 
+def make_proj(dso):
+    """``proj_small.npz``: the fused projections through the reference's own
+    ``linear`` (fp32 matmul cast to fp16), ``rms_norm`` (fp32 in and out, no
+    rounding between norm and rotation, as the fused Metal kernel),
+    ``dit_rope`` and ``apply_split_half_rope``, and the block's gated residual
+    update ``x + gate * out`` (fp32 residual, fp16 branch)."""
+    out = {}
+    images, tokens = 2, 64
+    x, w, qw, kw = inputs.proj_qkv(seed=21, images=images, tokens=tokens, k=256, q_heads=2, k_heads=2,
+                                   v_cols=256)
+    y = dso.linear(torch.from_numpy(x), torch.from_numpy(w))          # fp16 [128, 768]
+    m = y.shape[0]
+    q = y[:, :256].float().reshape(images, tokens, 2, 128)
+    k = y[:, 256:512].float().reshape(images, tokens, 2, 128)
+    qn = dso.rms_norm(q, torch.from_numpy(qw).float())
+    kn = dso.rms_norm(k, torch.from_numpy(kw).float())
+    rope = dso.dit_rope(8, 8, 1)                                       # 64 tokens
+    qr, kr = dso.apply_split_half_rope(qn, kn, rope)
+    v = y[:, 512:].float()
+    out["qkv_rope_out"] = torch.cat([qr.reshape(m, 256), kr.reshape(m, 256), v], dim=1).numpy()
+    out["qkv_rms_out"] = torch.cat([qn.reshape(m, 256), kn.reshape(m, 256), v], dim=1).numpy()
+    out["qkv_in_checksum"] = np.concatenate([checksum(x), checksum(w), checksum(qw), checksum(kw)])
+    out["qkv_meta"] = np.array([21, images, tokens, 256, 2, 2, 256], dtype=np.int64)
+    xg, wg, res, gate = inputs.proj_gate(seed=22, images=images, tokens=tokens, k=256, n=256)
+    branch = dso.linear(torch.from_numpy(xg), torch.from_numpy(wg)).float()
+    g = torch.from_numpy(gate)[torch.arange(m) // tokens]
+    out["gate_out"] = (torch.from_numpy(res) + g * branch).numpy()
+    out["gate_in_checksum"] = np.concatenate([checksum(xg), checksum(wg), checksum(res), checksum(gate)])
+    out["gate_meta"] = np.array([22, images, tokens, 256, 256], dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "proj_small.npz"), **out)
+
+
 def main():
     global REF
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="AnimaXS source checkout")
     ap.add_argument("--skip-large", action="store_true")
+    ap.add_argument("--only-proj", action="store_true", help="write proj_small.npz only")
     args = ap.parse_args()
     REF = load_reference(args.reference)
     dso, qco = REF
     torch.set_num_threads(os.cpu_count())
+    make_proj(dso)
+    if args.only_proj:
+        return
 
     # ---------------- RoPE tables ----------------
     rope = {}

@@ -174,3 +174,40 @@ def test_executor_mirror_errors_without_gpu():
     with pytest.raises(AttentionValidationError, match="token-major"):
         ex.make_desc(heads=2, query_count=4, key_count=4, head_dim=64,
                      layout=AttentionInputLayout.token_major(128))
+
+
+def _pdesc(lib, m=256, n=768, k=256, epilogue=1, **kw):
+    from animaxs_b200._lib import ProjDesc
+    d = ProjDesc()
+    assert lib.animaxs_proj_desc_init(ctypes.byref(d), m, n, k, epilogue) == 0
+    if epilogue == 1:
+        d.qk_norm, d.q_cols, d.k_cols = 1, 256, 256
+    if epilogue == 2:
+        d.gate = 0x6000
+    for key, val in kw.items():
+        setattr(d, key, val)
+    return d
+
+
+def _pvalidate(lib, d, ptrs=(0x1000, 0x2000, 0x3000)):
+    return lib.animaxs_proj_validate(None, ctypes.byref(d), *[ctypes.c_void_p(p) for p in ptrs])
+
+
+def test_projection_validation(lib):
+    """animaxs_proj_validate: shapes, alignment, head multiples, epilogue inputs."""
+    assert _pvalidate(lib, _pdesc(lib)) == 0
+    assert _pvalidate(lib, _pdesc(lib, epilogue=0)) == 0
+    assert _pvalidate(lib, _pdesc(lib, epilogue=2, n=256)) == 0
+    assert _pvalidate(lib, _pdesc(lib, m=0)) == -1
+    assert _pvalidate(lib, _pdesc(lib, k=100)) == -1                    # k % 8
+    assert _pvalidate(lib, _pdesc(lib), (0x1008, 0x2000, 0x3000)) == -1  # alignment
+    assert _pvalidate(lib, _pdesc(lib, x_stride=128)) == -1             # stride < k
+    assert _pvalidate(lib, _pdesc(lib, epilogue=3)) == -1
+    assert _pvalidate(lib, _pdesc(lib, q_cols=192)) == -2               # heads of 128
+    assert _pvalidate(lib, _pdesc(lib, q_cols=512, k_cols=512)) == -2   # q + k > n
+    assert _pvalidate(lib, _pdesc(lib, qk_norm=0)) == -1
+    assert _pvalidate(lib, _pdesc(lib, qk_norm=2)) == -1                # rope table missing
+    assert _pvalidate(lib, _pdesc(lib, qk_norm=2, rope_table=0x5000, rope_rows=256)) == 0
+    assert _pvalidate(lib, _pdesc(lib, qk_norm=2, rope_table=0x5000, rope_rows=255)) == -1
+    assert _pvalidate(lib, _pdesc(lib, epilogue=2, n=256, gate=None)) == -1
+    assert _pvalidate(lib, _pdesc(lib, epilogue=2, n=256, out_stride=258)) == -1  # fp32 rows: 16 B

@@ -148,3 +148,26 @@ def test_oracle_matches_reference_configs(name):
     np.testing.assert_allclose(got_in, g[name + "_in_checksum"], rtol=1e-9)
     out = case.oracle(rows=rows)
     np.testing.assert_allclose(out, g[name + "_out"], atol=3e-5, rtol=0)
+
+
+# ------------------------------------------------ fused projections (row f) --
+def test_projection_oracle_matches_reference():
+    """qkv_norm_projection / gate_add_projection against the reference's own
+    linear + rms_norm + dit_rope + apply_split_half_rope and its gated residual
+    update (tests/golden/proj_small.npz)."""
+    g = _npz("proj_small.npz")
+    seed, images, tokens, k, qh, kh, vc = (int(v) for v in g["qkv_meta"])
+    x, w, qw, kw = inputs.proj_qkv(seed, images=images, tokens=tokens, k=k, q_heads=qh, k_heads=kh, v_cols=vc)
+    np.testing.assert_allclose(np.concatenate([_checksum(x), _checksum(w), _checksum(qw), _checksum(kw)]),
+                               g["qkv_in_checksum"], rtol=1e-12)
+    table = ora.dit_rope_table(1, 8, 8)
+    for mode, key in (("rms_rope", "qkv_rope_out"), ("rms", "qkv_rms_out")):
+        got = ora.qkv_norm_projection(x, w, q_cols=qh * 128, k_cols=kh * 128, qk_norm=mode,
+                                      q_norm_weight=qw, k_norm_weight=kw, rope_table=table, tokens=tokens)
+        np.testing.assert_allclose(got, g[key], atol=2e-5, rtol=1e-5, err_msg=mode)
+    seed, images, tokens, k, n = (int(v) for v in g["gate_meta"])
+    xg, wg, res, gate = inputs.proj_gate(seed, images=images, tokens=tokens, k=k, n=n)
+    np.testing.assert_allclose(np.concatenate([_checksum(xg), _checksum(wg), _checksum(res), _checksum(gate)]),
+                               g["gate_in_checksum"], rtol=1e-12)
+    got = ora.gate_add_projection(res, xg, wg, gate, tokens=tokens)
+    np.testing.assert_allclose(got, g["gate_out"], atol=2e-5, rtol=1e-5)
