@@ -90,7 +90,7 @@ struct ProjParams {
   const float* gate;        // kProjGateAdd: [images][gate_stride] fp32
   long long gate_stride;
   int tiles_n;              // ceil(n / 256)
-  int tiles;                // ceil(m / 128) * tiles_n
+  int tiles;                // ceil(m / 256) * tiles_n (256 x 256 tiles, one per CTA pair)
   unsigned int* status;
 };
 cudaError_t launch_proj(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tout,

@@ -135,7 +135,7 @@ extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_de
   const bool f32_out = d->epilogue == ANIMAXS_PROJ_GATE_ADD;
   CUtensorMap ta, tb, tout;
   rc = make_tmap_2d(ctx, &ta, x, false, d->k, d->m, d->x_stride, 64, 128);
-  if (rc == ANIMAXS_OK) rc = make_tmap_2d(ctx, &tb, w, false, d->k, d->n, d->w_stride, 64, 256);
+  if (rc == ANIMAXS_OK) rc = make_tmap_2d(ctx, &tb, w, false, d->k, d->n, d->w_stride, 64, 128);
   if (rc == ANIMAXS_OK)
     rc = f32_out ? make_tmap_2d(ctx, &tout, out, true, d->n, d->m, d->out_stride, 32, 128)
                  : make_tmap_2d(ctx, &tout, out, false, d->n, d->m, d->out_stride, 64, 128);
@@ -167,7 +167,7 @@ extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_de
   p.gate = d->gate;
   p.gate_stride = d->gate_stride;
   p.tiles_n = (d->n + 255) / 256;
-  const long long tiles = static_cast<long long>((d->m + 127) / 128) * p.tiles_n;
+  const long long tiles = static_cast<long long>((d->m + 255) / 256) * p.tiles_n;  // 256 x 256 (a CTA pair)
   if (tiles > 0x7fffffffLL) return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "projection too large");
   p.tiles = static_cast<int>(tiles);
   p.status = ctx->d_status;

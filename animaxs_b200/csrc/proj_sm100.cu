@@ -22,16 +22,26 @@
 // A 128-column half of an output tile is exactly one head, so the norm and
 // the rotation need nothing beyond the thread's own row.
 //
-// Persistent: one CTA per SM walks 128 x 256 output tiles (row-major over the
-// tile grid, so concurrent CTAs share x rows and all of w stays in L2).  Six
-// warps: warp 0 TMA producer (x and w K-slices of 64 into a 4-stage ring),
-// warp 1 MMA issuer + TMEM owner (tcgen05.mma kind::f16, M 128, N 256, K 16:
-// 4 per stage), warps 4-11 epilogue (two threads per output row = TMEM lane,
-// each holding half of every head's columns).  Two
-// 256-column TMEM accumulators alternate, so a tile's epilogue runs while the
-// next tile accumulates.  Outputs leave through a 32 KiB shared-memory stage in
-// the tensor-store layout (TMA stores / reduce-adds; rows and columns past the
-// matrix are clipped by the tensor map).
+// CTA pairs.  A 128 x 256 tile per SM needs ~96 B/clk of operands from L2 at
+// full tensor rate, above what L2 delivers (~53 B/clk/SM measured), so two
+// CTAs of a cluster run as one tcgen05 CTA pair (cta_group::2) on 256 x 256
+// tiles: the pair leader issues M = 256, N = 256 MMAs whose A rows (x) come
+// from both CTAs and whose B (w) is split along N, so each CTA loads its own
+// 128 rows of x and half of the tile's w rows -- 32 KiB per K-slice of 64
+// instead of 48 for the same work.  The copies of both CTAs complete on the
+// leader's barriers (armed by the leader for both halves); MMA completions are
+// committed to both CTAs' barriers.
+//
+// Persistent: each pair walks 256 x 256 output tiles (row-major over the tile
+// grid).  Twelve warps per CTA: warp 0 TMA producer (6-stage ring), warp 1
+// TMEM owner and, in the leader, MMA issuer (4 MMAs per stage), warps 4-11
+// epilogue of the CTA's 128 rows (two threads per row = TMEM lane, each holding
+// half of every head's columns).  Two 256-column TMEM accumulators alternate,
+// so a tile's epilogue runs while the next tile accumulates; the epilogue
+// warps of both CTAs release an accumulator on the leader's barrier.  Outputs
+// leave through a 32 KiB shared-memory stage in the tensor-store layout (TMA
+// stores / reduce-adds; rows and columns past the matrix are clipped by the
+// tensor map).
 #include <atomic>
 
 #include "flash_common.cuh"
@@ -40,10 +50,10 @@
 namespace ax {
 namespace {
 
-constexpr int kBM = 128;
+constexpr int kBM = 128;   // rows per CTA (256 per pair)
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
+constexpr int kStages = 6;
 constexpr int kThreads = 384;       // warpgroup 0: TMA warp, MMA warp (+2 idle); warpgroups 1-2: epilogue
 constexpr int kEpiThreads = 256;
 // Register split (setmaxnreg): the kernel launches at the compiler's per-thread
@@ -53,8 +63,8 @@ constexpr int kEpiThreads = 256;
 // forever: build.py checks this against the ptxas report.
 #define AX_EPI_REGS 208
 #define AX_PROJ_OTHER_REGS 56
-constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KiB: one SW128 panel of 128 rows
-constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KiB: one SW128 panel of 256 rows
+constexpr uint32_t kABytes = kBM * kBK * 2;        // 16 KiB: this CTA's 128 rows of x
+constexpr uint32_t kBBytes = (kBN / 2) * kBK * 2;  // 16 KiB: this CTA's half of the tile's w rows
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kOut = kStages * kStageBytes;  // 192 KiB
 constexpr uint32_t kOutBytes = 32768;             // output stage
@@ -67,14 +77,14 @@ enum : int {
   kBarFull = 0,                      // +stage
   kBarEmpty = kBarFull + kStages,    // +stage
   kBarAccFull = kBarEmpty + kStages, // +accumulator
-  kBarAccEmpty = kBarAccFull + 2,    // +accumulator, 8 arrivals (epilogue warps)
+  kBarAccEmpty = kBarAccFull + 2,    // +accumulator, leader: 16 arrivals (epilogue warps of both CTAs)
   kBarDone = kBarAccEmpty + 2,
   kNumBars
 };
 constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 static_assert(kSlotAbort + 4 <= 256, "barrier block overflows its 256 bytes");
-constexpr uint32_t kIdesc = idesc_f16_f32(kBM, kBN, false);
+constexpr uint32_t kIdesc = idesc_f16_f32(2 * kBM, kBN, false);  // pair MMA: M 256, N 256
 constexpr uint32_t kEpiBar = 1;   // named barrier of the 8 epilogue warps
 
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
@@ -93,24 +103,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int k_blocks = (p.k + kBK - 1) / kBK;
+  // Cluster (2, 1, 1): rank 0 leads the pair; rank c holds rows [128c, 128c + 128)
+  // of every 256-row tile and w rows [128c, 128c + 128) of its 256 columns.
+  const int cid = static_cast<int>(cluster_ctarank());
+  const int pair = static_cast<int>(blockIdx.x) >> 1;
+  const int pairs = static_cast<int>(gridDim.x) >> 1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(BAR(i), (i >= kBarAccEmpty && i < kBarAccEmpty + 2) ? 8u : 1u);
+      mbar_init(BAR(i), (i >= kBarAccEmpty && i < kBarAccEmpty + 2) ? 16u : 1u);
     *abort_flag = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
-    tmem_alloc(bar0 + kSlotTmem, 512);
-    tmem_relinquish();
+    tmem_alloc2(bar0 + kSlotTmem, 512);
+    tmem_relinquish2();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     tma_prefetch_desc(&tm_out);
   }
+  // Both CTAs' barriers exist (and TMEM is allocated) before any copy or
+  // arrival targets the leader's.
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -119,23 +136,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      int armed[kStages] = {};
       uint32_t g = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
-        const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * kBN;
+      for (int t = pair; ok && t < p.tiles; t += pairs) {
+        const int m0 = (t / p.tiles_n) * 2 * kBM, n0 = (t % p.tiles_n) * kBN;
         for (int kb = 0; kb < k_blocks; ++kb, ++g) {
           const uint32_t st = g % kStages;
           if (!(ok = mbar_wait(BAR(kBarEmpty + st), ((g / kStages) & 1u) ^ 1u, abort_flag, p.status))) break;
           const uint32_t sa = base + st * kStageBytes;
-          mbar_arrive_expect_tx(BAR(kBarFull + st), kStageBytes);
-          tma_load_2d(sa, &tm_a, BAR(kBarFull + st), kb * kBK, m0);
-          tma_load_2d(sa + kABytes, &tm_b, BAR(kBarFull + st), kb * kBK, n0);
-          ++armed[st];
+          const uint32_t full = mapa_shared(BAR(kBarFull + st), 0);
+          if (cid == 0) mbar_arrive_expect_tx(BAR(kBarFull + st), 2 * kStageBytes);
+          tma_load_2d_pair(sa, &tm_a, full, kb * kBK, m0 + cid * kBM);
+          tma_load_2d_pair(sa + kABytes, &tm_b, full, kb * kBK, n0 + cid * (kBN / 2));
         }
       }
-      for (int st = 0; st < kStages; ++st)
-        if (armed[st]) mbar_wait_drain(BAR(kBarFull + st), (armed[st] - 1) & 1);
+      // The copies complete on the leader's barriers.  Normally every one was
+      // consumed by an MMA that retired before Done; after an abort, give the
+      // ones still in flight time to land before the CTA may exit.
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 100000ull) {
+        }
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -143,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;
     bool ok = true;
     int it = 0;
-    for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++it) {
+    for (int t = pair; cid == 0 && ok && t < p.tiles; t += pairs, ++it) {
       const uint32_t acc = it & 1;
       // The epilogue has drained this accumulator (its previous use, two tiles ago).
       if (!(ok = mbar_wait_warp(BAR(kBarAccEmpty + acc), ((it >> 1) & 1u) ^ 1u, abort_flag, p.status))) break;
@@ -157,14 +179,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t a0 = sw128_desc(sa, 16, 1024), b0 = sw128_desc(sa + kABytes, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_f16_ss_warp(d, a0 + static_cast<uint64_t>(kk * 2), b0 + static_cast<uint64_t>(kk * 2), kIdesc,
-                           (kb > 0 || kk > 0) ? 1u : 0u);
-        tc_commit_warp(BAR(kBarEmpty + st));
+          umma2_f16_ss_warp(d, a0 + static_cast<uint64_t>(kk * 2), b0 + static_cast<uint64_t>(kk * 2), kIdesc,
+                            (kb > 0 || kk > 0) ? 1u : 0u);
+        tc_commit2_mc_warp(BAR(kBarEmpty + st), 3);
       }
       if (!ok) break;
-      tc_commit_warp(BAR(kBarAccFull + acc));
+      tc_commit2_mc_warp(BAR(kBarAccFull + acc), 3);
     }
-    tc_commit_warp(BAR(kBarDone));
+    // Every MMA of the pair retires before either CTA releases TMEM or exits.
+    if (cid == 0) tc_commit2_mc_warp(BAR(kBarDone), 3);
     mbar_wait_drain(BAR(kBarDone), 0);
     __syncwarp();
   }
@@ -184,11 +207,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = (et == 0);                  // issues the tensor stores
     const uint32_t sOut = base + kOut;
     volatile float* xss = reinterpret_cast<volatile float*>(gbase + kXss);  // [2][128] sums of squares
+    const uint32_t acc_empty0 = mapa_shared(BAR(kBarAccEmpty), 0);  // the leader's
     bool ok = true;
     int it = 0;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++it) {
+    for (int t = pair; t < p.tiles; t += pairs, ++it) {
       const uint32_t acc = it & 1;
-      const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * kBN;
+      const int m0 = (t / p.tiles_n) * 2 * kBM + cid * kBM, n0 = (t % p.tiles_n) * kBN;
       const int row = m0 + r;
       bool got = ok && mbar_wait(BAR(kBarAccFull + acc), (it >> 1) & 1u, abort_flag, p.status);
       got = __all_sync(0xffffffffu, got);
@@ -232,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Both heads are in registers: the accumulator may take the next tile.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(BAR(kBarAccEmpty + acc));
+          if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * acc);
         }
         if (p.mode == kProjGateAdd) {
           // fp32 through the stage in two 64-column rounds, each two 32-column
@@ -335,11 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader) tma_store_wait_all();
   }
 
+  // Neither CTA of the pair releases TMEM while the other may still use it.
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc2(tmem, 512);
   }
 #undef BAR
 }
@@ -384,8 +409,21 @@ cudaError_t launch_proj(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     sm_count[dev & 63].store(sms, std::memory_order_relaxed);
   }
   if (p.tiles <= 0) return cudaSuccess;
-  const int grid = p.tiles < sms ? p.tiles : sms;
-  proj_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tout, p);
+  const int pairs = p.tiles < sms / 2 ? p.tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, proj_sm100_kernel, ta, tb, tout, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -141,6 +141,17 @@ __device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, uint32_t src
 __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// 2-D tiled tensor load issued by one CTA of a tcgen05 CTA pair: the data lands
+// in this CTA's shared memory and the byte count completes on `bar_leader`, the
+// pair leader's mbarrier (a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_leader,
+                                                 int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(bar_leader), "r"(c0), "r"(c1)
+      : "memory");
+}
 
 // 4-D tiled tensor store from shared memory (bulk-group completion); elements
 // outside the tensor's extents are not written.
@@ -249,6 +260,54 @@ __device__ __forceinline__ void tc_commit_warp(uint32_t bar) {
       "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
           bar)
       : "memory");
+}
+
+// CTA-pair (cta_group::2) forms, issued by the pair leader: one M = 256 MMA
+// whose A rows 0-127 / 128-255 and D rows come from / go to the two CTAs
+// (same shared-memory and TMEM addresses in both) and whose B is split along
+// N, the first N/2 in the leader, the rest in its peer.
+__device__ __forceinline__ void umma2_f16_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %4, 0;\n\t"
+      "@p tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma2_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %4, 0;\n\t"
+      "@p tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the barrier at `bar` (a shared::cta offset) in every CTA of
+// `cta_mask` when the pair's prior tcgen05 ops complete.
+__device__ __forceinline__ void tc_commit2_mc_warp(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand.
@@ -374,6 +433,12 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
 }
 
 // ------------------------------------------------- thread-block clusters --
+// Arrive on an mbarrier of another CTA of the cluster (shared::cluster address),
+// releasing this thread's prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
