@@ -171,7 +171,23 @@ extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_de
   if (tiles > 0x7fffffffLL) return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "projection too large");
   p.tiles = static_cast<int>(tiles);
   p.status = ctx->d_status;
+  // Kernel timing (animaxs_attn_set_kernel_timing) brackets this launch too.
+  cudaEvent_t ev_stop = nullptr;
+  if (ctx->timing) {
+    while (ctx->events.size() < ctx->events_used + 2) {
+      cudaEvent_t ev;
+      cudaError_t ce = cudaEventCreate(&ev);
+      if (ce != cudaSuccess) return ax_cuda_fail(ctx, ce, "timing event");
+      ctx->events.push_back(ev);
+    }
+    cudaEventRecord(ctx->events[ctx->events_used], static_cast<cudaStream_t>(stream));
+    ev_stop = ctx->events[ctx->events_used + 1];
+  }
   cudaError_t e = ax::launch_proj(ta, tb, tout, p, static_cast<cudaStream_t>(stream));
+  if (ev_stop != nullptr && e == cudaSuccess) {
+    cudaEventRecord(ev_stop, static_cast<cudaStream_t>(stream));
+    ctx->events_used += 2;
+  }
   if (e != cudaSuccess) {
     int regs = 0, threads = 0, ss = 0, sd = 0;
     ax::proj_kernel_attributes(&regs, &threads, &ss, &sd);

@@ -553,11 +553,139 @@ def run_vae(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+D_MODEL = HEADS * HD                               # 2048
+QKV_FLOPS = 2.0 * S_SELF * 3 * D_MODEL * D_MODEL    # fused q|k|v projection, per image
+PROJ_FLOPS = 2.0 * S_SELF * D_MODEL * D_MODEL       # one 2048 x 2048 projection, per image
+BLOCK_PROJ_FLOPS = QKV_FLOPS + 3 * PROJ_FLOPS       # self q|k|v, self out, cross q, cross out
+
+
+def run_proj(args, rank, world, local_rank):
+    """The projections on either side of DiT attention, fused
+    (DiTBlockExecutor.swift:1097-1131, 1223-1236): per block, for a batch of 8
+    images -- self q|k|v with q/k RMSNorm + 3-D RoPE in the epilogue, the self
+    out-projection + gated residual (fp32 residual += fp16 branch x gate), the
+    cross q projection + RMSNorm and the cross out-projection + gated residual
+    (the cross K/V come from the reference's CrossKVCache and are not
+    re-projected).  One step = 224 blocks (28 blocks x 8 Euler steps) of one
+    batch, like config 4; value = images/s; random-init weights of the DiT's
+    shapes (2048 -> 6144 / 2048)."""
+    import torch
+    import torch.distributed as dist
+
+    import animaxs_b200 as ax
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ex = ax.AttentionExecutor(local_rank)
+    pj = ax.ProjectionExecutor(ex)
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(2024 + rank)
+    m = BATCH * S_SELF
+    xs = [torch.randn(m, D_MODEL, generator=g, device=device).half() for _ in range(POOL_BLOCKS)]
+    w_qkv = (torch.randn(3 * D_MODEL, D_MODEL, generator=g, device=device) / D_MODEL ** 0.5).half()
+    w_so, w_cq, w_co = ((torch.randn(D_MODEL, D_MODEL, generator=g, device=device) / D_MODEL ** 0.5).half()
+                        for _ in range(3))
+    qw = (1 + 0.1 * torch.randn(HD, generator=g, device=device)).half()
+    kw = (1 + 0.1 * torch.randn(HD, generator=g, device=device)).half()
+    rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).to(device)
+    residual = torch.zeros(m, D_MODEL, device=device)
+    gates = 0.1 * torch.randn(2, BATCH, D_MODEL, generator=g, device=device)
+    qkv = torch.empty(m, 3 * D_MODEL, dtype=torch.float16, device=device)
+    q_cross = torch.empty(m, D_MODEL, dtype=torch.float16, device=device)
+
+    def block(i):
+        x = xs[i % POOL_BLOCKS]
+        pj.qkv(x, w_qkv, qkv, q_cols=D_MODEL, k_cols=D_MODEL, qk_norm="rms_rope", q_norm_weight=qw,
+               k_norm_weight=kw, rope_table=rope, tokens=S_SELF, stream=stream)
+        pj.out_gate_add(x, w_so, residual, gates[0], tokens=S_SELF, stream=stream)
+        pj.qkv(x, w_cq, q_cross, q_cols=D_MODEL, k_cols=0, qk_norm="rms", q_norm_weight=qw, stream=stream)
+        pj.out_gate_add(x, w_co, residual, gates[1], tokens=S_SELF, stream=stream)
+
+    def step():
+        for i in range(CALLS_PER_IMAGE):
+            block(i)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ex.synchronize(stream)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    ex.set_kernel_timing(True)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ex.set_kernel_timing(False)
+    n_kern, kern_total_ms, kern_max_ms = ex.kernel_timing()
+    ex.synchronize(stream)
+    el = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([el], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    if rank != 0:
+        return
+    peak_burst, peak_sust, _, peak_kind = peaks()
+    images = args.steps * world * BATCH
+    flops = args.steps * CALLS_PER_IMAGE * BATCH * BLOCK_PROJ_FLOPS
+    avg_kern = kern_total_ms / n_kern if n_kern else float("nan")
+    achieved = BATCH * BLOCK_PROJ_FLOPS / 4 / (avg_kern / 1e3) / 1e12   # mean over the 4 launches
+    line = {
+        "metric": "DiT attention projections throughput, 8-step 1024x1024 workload (fused q|k|v "
+                  "rms+rope3d, out-proj + gated residual, cross q rms, cross out-proj + gated residual)",
+        "value": images / (el / 1e3), "unit": "img/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic, random-init weights",
+        "config": {"workload": "proj: 224 blocks x batch 8, x [32768, 2048] -> q|k|v [32768, 6144] and 3 x "
+                               "[32768, 2048] projections", "parallelism": f"batch-shard x{world}",
+                   "l2": f"x cycled over {POOL_BLOCKS} x 128 MiB (> 126 MB L2)"},
+        "tflops_per_gpu": flops / (el / 1e3) / 1e12,
+        "roofline": {"kernel": "proj_sm100_kernel (CTA-pair tcgen05 GEMM, fused epilogues; mean of the 4 "
+                               "launches of a block)",
+                     "bound": "tensor", "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                     "frac": achieved / peak_sust, "peak_kind": f"{peak_kind} bf16 dense, sustained",
+                     "frac_of_burst_peak": achieved / peak_burst, "avg_launch_ms": avg_kern,
+                     "max_launch_ms": kern_max_ms, "launches_timed": n_kern, "traffic": None},
+        "clocks": clocks,
+        "gpu_launches": args.steps * CALLS_PER_IMAGE * 5,   # 4 GEMMs + the RoPE-table re-layout
+        "e2e": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def profile_kernel(args):
     import torch
 
     import animaxs_b200 as ax
     ex = ax.AttentionExecutor(0)
+    if args.workload == "proj":
+        # warmup + steps fused q|k|v (rms + rope3d) projections of a batch of 4 images
+        pj = ax.ProjectionExecutor(ex)
+        g = torch.Generator(device="cuda").manual_seed(5)
+        m = 4 * S_SELF
+        x = torch.randn(m, D_MODEL, generator=g, device="cuda").half()
+        w = (torch.randn(3 * D_MODEL, D_MODEL, generator=g, device="cuda") / D_MODEL ** 0.5).half()
+        out = torch.empty(m, 3 * D_MODEL, dtype=torch.float16, device="cuda")
+        nw = torch.ones(HD, dtype=torch.float16, device="cuda")
+        rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).cuda()
+        for _ in range(args.warmup + args.steps):
+            pj.qkv(x, w, out, q_cols=D_MODEL, k_cols=D_MODEL, q_norm_weight=nw, k_norm_weight=nw,
+                   rope_table=rope, tokens=S_SELF)
+        torch.cuda.synchronize()
+        ex.synchronize()
+        print("profile-kernel done", flush=True)
+        return
     if args.workload == "vae":
         # warmup + steps VAE middle-attention calls on distinct images (> L2 in total)
         g = torch.Generator(device="cuda").manual_seed(5)
@@ -592,10 +720,11 @@ def main():
     ap.add_argument("--impl", default="animaxs", choices=["animaxs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae"],
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae", "proj"],
                     help="cfg4 (default): the 8-step DiT workload, batch-sharded; cfg5: the "
                          "16384-token self-attention, heads sharded + one NCCL all-gather; vae: "
-                         "the VAE decoder's middle attention (one head of 384), images per rank")
+                         "the VAE decoder's middle attention (one head of 384), images per rank; "
+                         "proj: the fused projections around DiT attention")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only run the fused rms+rope3d self-attention (prologue + flash kernel) "
                          "on a batch-4 4096-token case (192 MiB of inputs, > L2), or with "
@@ -624,6 +753,8 @@ def main():
             run_cfg5(args, rank, world, local_rank)
         elif args.workload == "vae":
             run_vae(args, rank, world, local_rank)
+        elif args.workload == "proj":
+            run_proj(args, rank, world, local_rank)
         else:
             run_gpu(args, rank, world, local_rank)
     finally:

@@ -287,7 +287,8 @@ int animaxs_proj_desc_init(animaxs_proj_desc* desc, int m, int n, int k, int epi
 /* Validate exactly as animaxs_proj_forward does, without a GPU. */
 int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, const void* x,
                           const void* w, const void* out);
-/* Enqueue the fused projection on `stream`. */
+/* Enqueue the fused projection on `stream` (bracketed by CUDA events, like
+ * the attention kernel, while animaxs_attn_set_kernel_timing is on). */
 int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, const void* x,
                          const void* w, void* out, void* stream);
 
