@@ -41,8 +41,9 @@
 // across the whole persistent loop.
 #include <atomic>
 
-#include "kernels.h"
+#include "api_internal.h"
 #include "flash_common.cuh"
+#include "kernels.h"
 
 namespace ax {
 namespace {
@@ -61,7 +62,10 @@ struct Smem {
   static constexpr uint32_t kK = kQ + 2 * kTile;
   static constexpr uint32_t kV = kK + kKStages * kTile;
   static constexpr uint32_t kBar = kV + kVStages * kTile;
-  static constexpr uint32_t kBytes = kBar + 256 + 1024;  // + barriers + alignment slack
+  // Output stage: per softmax warp, 32 rows x 64 columns fp16 (4 KiB) in the
+  // tensor-store layout; 8 warps.
+  static constexpr uint32_t kStage = kBar + 1024;
+  static constexpr uint32_t kBytes = kStage + 8 * 4096 + 1024;  // + alignment slack
 };
 constexpr int kThreads = 384;  // warpgroups: softmax A, softmax B, MMA/TMA (+2 idle warps)
 
@@ -134,7 +138,8 @@ template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const AttnFwdParams p) {
+                          const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_o, const AttnFwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -188,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
   }
   tc_fence_before();
   __syncthreads();
@@ -451,26 +457,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(BAR(kBarODone + X), eX & 1u, abort_flag, p.status);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
+          // Normalise and store O: each warp stages its 32 rows, 64 columns at a
+          // time, in the tensor-store layout (16-byte unit u of row r at unit
+          // u ^ (r % 8)) and its lane 0 writes them with one TMA store (rows
+          // past q_len are clipped by the tensor map).  No cross-warp sync.
           tc_fence_after();
           const float inv_l = 1.f / l;
-          __half* orow = p.o + static_cast<long long>(I.b) * p.o_batch +
-                         static_cast<long long>(row) * p.o_tok +
-                         static_cast<long long>(I.h - p.o_head_base) * p.o_head;
+          const uint32_t stage = base + L::kStage + static_cast<uint32_t>(warp) * 4096u + lane * 128u;
 #pragma unroll
-          for (int c4 = 0; c4 < HD / 32; ++c4) {
-            uint32_t o[32];
-            tmem_ld32(o_addr + c4 * 32, o);
-            tmem_ld_wait(o);
-            if (row < p.q_len) {
+          for (int rd = 0; rd < HD / 64; ++rd) {
+            uint32_t o[2][32];
+            tmem_ld32(o_addr + rd * 64, o[0]);
+            tmem_ld32(o_addr + rd * 64 + 32, o[1]);
+            tmem_ld_wait(o[0]);
+            asm volatile("" : AX_RW32(o[1])::"memory");
+            // The stage's previous store (last round or item) has been read.
+            if (lane == 0) tma_store_wait_read();
+            __syncwarp();
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                uint4 v;
-                v.x = pack_half2(__uint_as_float(o[i * 8 + 0]) * inv_l, __uint_as_float(o[i * 8 + 1]) * inv_l);
-                v.y = pack_half2(__uint_as_float(o[i * 8 + 2]) * inv_l, __uint_as_float(o[i * 8 + 3]) * inv_l);
-                v.z = pack_half2(__uint_as_float(o[i * 8 + 4]) * inv_l, __uint_as_float(o[i * 8 + 5]) * inv_l);
-                v.w = pack_half2(__uint_as_float(o[i * 8 + 6]) * inv_l, __uint_as_float(o[i * 8 + 7]) * inv_l);
-                *reinterpret_cast<uint4*>(orow + c4 * 32 + i * 8) = v;
-              }
+            for (int u = 0; u < 8; ++u) {
+              const uint32_t* ov = &o[u >> 2][(u & 3) * 8];
+              st_shared_v4(stage + (((u ^ (lane & 7))) << 4),
+                           pack_half2(__uint_as_float(ov[0]) * inv_l, __uint_as_float(ov[1]) * inv_l),
+                           pack_half2(__uint_as_float(ov[2]) * inv_l, __uint_as_float(ov[3]) * inv_l),
+                           pack_half2(__uint_as_float(ov[4]) * inv_l, __uint_as_float(ov[5]) * inv_l),
+                           pack_half2(__uint_as_float(ov[6]) * inv_l, __uint_as_float(ov[7]) * inv_l));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_4d(&tm_o, base + L::kStage + static_cast<uint32_t>(warp) * 4096u, 64 * rd,
+                           I.q0 + X * kTileM + (warp & 3) * 32, I.h - p.o_head_base, I.b);
+              tma_store_commit();
             }
           }
         }
@@ -480,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (warp < 8 && lane == 0) tma_store_wait_all();  // the output stores have completed
   tc_fence_before();
   __syncthreads();
   if (warp == 8) {
@@ -522,7 +541,12 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   q.n_items = static_cast<int>(items);
   const int grid = static_cast<int>(items < sms ? items : sms);
-  attn_fwd_sm100_kernel<HD><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, q);
+  // Output view [batch][heads][q_len][HD] for the tensor stores (box 64 x 32).
+  CUtensorMap to;
+  if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
+                   p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
+    return cudaErrorInvalidValue;
+  attn_fwd_sm100_kernel<HD><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
   return cudaGetLastError();
 }
 
