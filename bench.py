@@ -47,9 +47,9 @@ IMAGE_FLOPS = CALLS_PER_IMAGE * (SELF_FLOPS + CROSS_FLOPS)
 BATCH = 8                                         # images per GPU per step (config 4)
 POOL_BLOCKS = 3                                   # distinct resident input sets (> L2)
 # DRAM bytes (read + write) of one batch-8 self-attention flash launch: the ncu
-# capture in profiles/attn_fwd_sm100_selfattn4096_batch4.md measured 245.8 MB
+# capture in profiles/attn_fwd_sm100_selfattn4096_batch4.md measured 245.5 MB
 # for batch 4; traffic scales with the batch.
-TRAFFIC_PER_LAUNCH_MB = 491.6
+TRAFFIC_PER_LAUNCH_MB = 491.0
 
 METRIC = ("DiT attention throughput, 8-step 1024x1024 workload "
           "(28 blocks x 8 steps x [4096-tok self rms+rope3d + 4096x512 cross rms])")
