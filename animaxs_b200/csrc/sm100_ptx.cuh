@@ -276,16 +276,6 @@ __device__ __forceinline__ void umma2_f16_ss_warp(uint32_t d_tmem, uint64_t a_de
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma2_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                  uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "elect.sync _|p, 0xffffffff;\n\t"
-      "setp.ne.b32 q, %4, 0;\n\t"
-      "@p tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, q;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // Arrive once on the barrier at `bar` (a shared::cta offset) in every CTA of
 // `cta_mask` when the pair's prior tcgen05 ops complete.
 __device__ __forceinline__ void tc_commit2_mc_warp(uint32_t bar, uint16_t cta_mask) {
