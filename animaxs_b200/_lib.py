@@ -116,6 +116,7 @@ SIGNATURES = {
     "animaxs_comm_destroy": (_I, [_P]),
     "animaxs_attn_forward_head_sharded": (_I, [_P, _P, _DESC, _P, _P, _P, _P, _P]),
     "animaxs_attn_forward_noalloc": (_I, [_DESC, _P, _P, _P, _P, _P]),
+    "animaxs_attn_selftest_wait_timeout": (_I, [_P, _I64, _P]),
     "animaxs_proj_desc_init": (_I, [ctypes.POINTER(ProjDesc), _I, _I, _I, _I]),
     "animaxs_proj_validate": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P]),
     "animaxs_proj_forward": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P, _P]),

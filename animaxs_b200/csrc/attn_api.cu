@@ -19,6 +19,7 @@
 #include "../../include/animaxs_attn.h"
 #include "api_internal.h"
 #include "kernels.h"
+#include "sm100_ptx.cuh"
 
 using ax::AttnFwdParams;
 using ax::NormJob;
@@ -474,6 +475,39 @@ extern "C" int animaxs_attn_synchronize(animaxs_attn_ctx* ctx, void* stream) {
   if (status & ax::kStatusTimeoutBit)
     return ax_set_error(ctx, ANIMAXS_ERR_TIMEOUT, "a bounded device-side wait expired");
   if (status != 0) return ax_set_error(ctx, ANIMAXS_ERR_CUDA, "device status 0x%x", status);
+  return ok(ctx);
+}
+
+// ------------------------------------------------------ failure detection --
+namespace {
+// One thread waits, through the kernels' bounded mbarrier wait, on a phase
+// that nothing completes; after `limit_ns` it sets the timeout status bit and
+// returns, as an aborting kernel does.
+__global__ void selftest_wait_kernel(unsigned int* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ax::mbar_init(ax::smem_u32(&bar), 1);
+    abort_flag = 0;
+    ax::mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ax::mbar_wait_for(ax::smem_u32(&bar), 0, &abort_flag, status, limit_ns);
+}
+}  // namespace
+
+extern "C" int animaxs_attn_selftest_wait_timeout(animaxs_attn_ctx* ctx, int64_t timeout_ns, void* stream) {
+  if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
+  if (timeout_ns <= 0 || timeout_ns > 10'000'000'000LL)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "self-test timeout must be in (0, 10 s]");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ctx->device);
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      ctx->d_status, static_cast<unsigned long long>(timeout_ns));
+  cudaError_t e = cudaGetLastError();
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "self-test launch");
   return ok(ctx);
 }
 

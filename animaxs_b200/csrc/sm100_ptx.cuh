@@ -61,9 +61,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with `parity` to complete.  Returns false (and leaves the
-// abort flag set) on timeout or when another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t* status) {
+// abort flag set) after `limit_ns` or when another role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                              uint32_t* status, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
@@ -71,13 +71,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 15u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > ANIMAXS_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         if (status) atomicOr(status, kStatusTimeout);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t* status) {
+  return mbar_wait_for(bar, parity, abort_flag, status, ANIMAXS_WAIT_TIMEOUT_NS);
 }
 
 // Wait bounded by time only (the abort flag is ignored): used where in-flight

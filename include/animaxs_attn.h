@@ -241,6 +241,17 @@ int animaxs_gqa_kv_head(int query_head, int heads, int kv_heads);
 int animaxs_attn_forward_noalloc(const animaxs_attn_desc* desc, const void* q, const void* k,
                                  const void* v, void* o, void* stream);
 
+/* Failure-detection self-test: enqueue one kernel whose only thread waits,
+ * through the same bounded device-side wait every kernel here uses, on a
+ * barrier phase that nothing completes; after `timeout_ns` (<= 10 s) it sets
+ * the context's status word and returns, exactly as a kernel whose wait ran
+ * out does.  The next animaxs_attn_synchronize on the stream then returns
+ * ANIMAXS_ERR_TIMEOUT (and clears the status); the context stays usable.
+ * Nothing faults or hangs.  Counterpart of the reference's numerical-failure
+ * detection surfacing a GPU error through `completed.error`
+ * (AttentionExecutor.swift:771). */
+int animaxs_attn_selftest_wait_timeout(animaxs_attn_ctx* ctx, int64_t timeout_ns, void* stream);
+
 /* ---- Fused attention projections ------------------------------------------
  * The GEMMs on either side of DiT attention, each with its elementwise step
  * fused into the epilogue (one kernel per call).  The reference encodes them

@@ -211,3 +211,8 @@ def test_projection_validation(lib):
     assert _pvalidate(lib, _pdesc(lib, qk_norm=2, rope_table=0x5000, rope_rows=255)) == -1
     assert _pvalidate(lib, _pdesc(lib, epilogue=2, n=256, gate=None)) == -1
     assert _pvalidate(lib, _pdesc(lib, epilogue=2, n=256, out_stride=258)) == -1  # fp32 rows: 16 B
+
+
+def test_selftest_rejects_bad_timeout(lib):
+    """The failure-detection self-test validates its limit before touching a device."""
+    assert lib.animaxs_attn_selftest_wait_timeout(None, 1000, None) == -1

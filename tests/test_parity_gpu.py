@@ -344,3 +344,21 @@ def test_rejects_unsupported(ex):
                    key_value_heads=1, layout=AttentionInputLayout.token_major(128))
     with pytest.raises(AttentionValidationError, match="out of bounds"):
         ex.execute(buf, buf, buf, buf, heads=1, query_count=8, key_count=4, head_dim=128)
+
+
+# ------------------------------------------------------- failure detection --
+def test_bounded_wait_reports_timeout_and_context_survives(ex):
+    """A device-side wait that runs out (the self-test kernel waits on a
+    barrier phase nothing completes, limit 50 ms) sets the status word:
+    synchronize reports ANIMAXS_ERR_TIMEOUT, clears it, and the same context
+    then runs attention correctly."""
+    import torch
+    from animaxs_b200 import AttentionTimeoutError
+    stream = torch.cuda.current_stream()
+    rc = ex._lib.animaxs_attn_selftest_wait_timeout(ex.handle, 50_000_000, stream.cuda_stream)
+    assert rc == 0
+    with pytest.raises(AttentionTimeoutError, match="bounded device-side wait"):
+        ex.synchronize(stream)
+    ex.synchronize(stream)  # status cleared
+    case = inputs.dit_cross(seed=3, q_len=300, kv_len=200, heads=2, kv_valid=None)
+    assert_parity(run_case(ex, case), case.oracle(), what="after a reported timeout")
