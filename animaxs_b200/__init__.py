@@ -11,4 +11,4 @@ from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError, 
                    AttentionValidationError, LIB_PATH, lib)
 from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  # noqa: F401
                        DitRoPE, GqaHeadMapping, adapter_rope, qwen_rope)
-from .projection import ProjectionExecutor  # noqa: F401,E402
+from .projection import ProjectionExecutor, QuantizedWeight  # noqa: F401,E402

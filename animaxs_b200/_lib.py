@@ -80,12 +80,14 @@ class ProjDesc(ctypes.Structure):
         ("epilogue", ctypes.c_int32), ("tokens", ctypes.c_int32), ("qk_norm", ctypes.c_int32),
         ("q_cols", ctypes.c_int32), ("k_cols", ctypes.c_int32), ("rope_rows", ctypes.c_int32),
         ("q_norm_weight", ctypes.c_void_p), ("k_norm_weight", ctypes.c_void_p),
-        ("rope_table", ctypes.c_void_p), ("eps", ctypes.c_float), ("reserved0", ctypes.c_int32),
+        ("rope_table", ctypes.c_void_p), ("eps", ctypes.c_float), ("w_storage", ctypes.c_int32),
         ("gate", ctypes.c_void_p), ("gate_stride", ctypes.c_int64),
+        ("w_scale", ctypes.c_void_p), ("w_zero", ctypes.c_void_p), ("w_packed_stride", ctypes.c_int64),
     ]
 
 
 PROJ_STORE, PROJ_QKV_NORM, PROJ_GATE_ADD = 0, 1, 2
+WEIGHT_FP16, WEIGHT_W8, WEIGHT_W4 = 0, 1, 2
 
 # name -> (restype, argtypes); every symbol the header declares.
 _P = ctypes.c_void_p
@@ -120,6 +122,7 @@ SIGNATURES = {
     "animaxs_proj_desc_init": (_I, [ctypes.POINTER(ProjDesc), _I, _I, _I, _I]),
     "animaxs_proj_validate": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P]),
     "animaxs_proj_forward": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P, _P]),
+    "animaxs_dequant_to_half": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I64, _I64, _P]),
 }
 
 _lib = None

@@ -99,4 +99,10 @@ int proj_kernel_attributes(int* regs, int* max_threads, int* smem_static, int* s
 // [rows][64][2][2] table blocks -> [64][rows] (cos, sin) pairs in `out` (rows*512 bytes).
 cudaError_t launch_rope_pairs(const float* table, void* out, int rows, cudaStream_t stream);
 
+// W8 (bits 8) / W4 (bits 4) codes + fp16 scale/zero per row and 64 columns ->
+// fp16 [rows][out_stride] (dequant_sm100.cu).
+cudaError_t launch_dequant(int bits, const void* packed, const void* scale, const void* zero, void* out,
+                           int rows, int k, int64_t packed_stride, int64_t out_stride, int sms,
+                           cudaStream_t stream);
+
 }  // namespace ax

@@ -60,12 +60,15 @@ int proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void*
   if (d->epilogue < ANIMAXS_PROJ_STORE || d->epilogue > ANIMAXS_PROJ_GATE_ADD)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown projection epilogue %d", d->epilogue);
   const bool f32_out = d->epilogue == ANIMAXS_PROJ_GATE_ADD;
-  if (d->k % 8 != 0 || d->x_stride < d->k || d->x_stride % 8 != 0 || d->w_stride < d->k ||
-      d->w_stride % 8 != 0 || d->out_stride < d->n || d->out_stride % (f32_out ? 4 : 8) != 0 ||
-      !aligned16(x) || !aligned16(w) || !aligned16(out))
+  // W8/W4 codes are decoded into an aligned fp16 copy first: only an fp16
+  // weight is read by the GEMM's tensor map (w_stride is then unused).
+  const bool fp16_w = d->w_storage == ANIMAXS_WEIGHT_FP16;
+  if (d->k % 8 != 0 || d->x_stride < d->k || d->x_stride % 8 != 0 ||
+      (fp16_w && (d->w_stride < d->k || d->w_stride % 8 != 0 || !aligned16(w))) || d->out_stride < d->n ||
+      d->out_stride % (f32_out ? 4 : 8) != 0 || !aligned16(x) || !aligned16(out))
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
                         "projection requires 16-byte-aligned buffers and row strides, k a multiple of 8");
-  if (d->x_stride >= (int64_t{1} << 38) || d->w_stride >= (int64_t{1} << 38) ||
+  if (d->x_stride >= (int64_t{1} << 38) || (fp16_w && d->w_stride >= (int64_t{1} << 38)) ||
       d->out_stride >= (int64_t{1} << 38))
     return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "projection byte size overflow");
   if (!(d->eps >= 0.f) || !std::isfinite(d->eps))
@@ -89,6 +92,37 @@ int proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void*
     if (d->gate == nullptr || d->gate_stride < d->n)
       return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "GATE_ADD needs a gate with gate_stride >= n");
   }
+  if (d->w_storage != ANIMAXS_WEIGHT_FP16) {
+    if (d->w_storage != ANIMAXS_WEIGHT_W8 && d->w_storage != ANIMAXS_WEIGHT_W4)
+      return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown weight storage %d", d->w_storage);
+    const int64_t need = d->w_storage == ANIMAXS_WEIGHT_W4 ? (int64_t{d->k} + 1) / 2 : d->k;
+    if (d->w_scale == nullptr || d->w_zero == nullptr || d->w_packed_stride < need ||
+        reinterpret_cast<uintptr_t>(d->w_scale) % 2 != 0 || reinterpret_cast<uintptr_t>(d->w_zero) % 2 != 0)
+      return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
+                          "W8/W4 weights need fp16 scale and zero and w_packed_stride >= %lld bytes",
+                          static_cast<long long>(need));
+    if (d->w_packed_stride >= (int64_t{1} << 40) ||
+        static_cast<int64_t>(d->n) * d->k >= (int64_t{1} << 40))
+      return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "projection byte size overflow");
+  }
+  return ANIMAXS_OK;
+}
+
+int dequant_validate(animaxs_attn_ctx* ctx, int bits, const void* packed, const void* scale, const void* zero,
+                     const void* out, int rows, int k, int64_t packed_stride, int64_t out_stride) {
+  if (bits != 4 && bits != 8) return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "bits must be 4 or 8");
+  if (packed == nullptr || scale == nullptr || zero == nullptr || out == nullptr)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "dequant buffers must not be null");
+  if (rows <= 0 || k <= 0) return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "invalid dequant shape");
+  const int64_t need = bits == 4 ? (int64_t{k} + 1) / 2 : k;
+  if (packed_stride < need || out_stride < k)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG,
+                        "packed_stride must be >= %lld bytes and out_stride >= k", static_cast<long long>(need));
+  if (reinterpret_cast<uintptr_t>(scale) % 2 != 0 || reinterpret_cast<uintptr_t>(zero) % 2 != 0 ||
+      reinterpret_cast<uintptr_t>(out) % 2 != 0)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "scale, zero and out must be 2-byte aligned");
+  if (packed_stride >= (int64_t{1} << 40) || out_stride >= (int64_t{1} << 40))
+    return ax_set_error(ctx, ANIMAXS_ERR_OVERFLOW, "dequant byte size overflow");
   return ANIMAXS_OK;
 }
 
@@ -117,6 +151,23 @@ extern "C" int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_d
   return rc;
 }
 
+extern "C" int animaxs_dequant_to_half(animaxs_attn_ctx* ctx, int bits, const void* packed, const void* scale,
+                                       const void* zero, void* out, int rows, int k, int64_t packed_stride,
+                                       int64_t out_stride, void* stream) {
+  if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
+  int rc = dequant_validate(ctx, bits, packed, scale, zero, out, rows, k, packed_stride, out_stride);
+  if (rc != ANIMAXS_OK) return rc;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != ctx->device) cudaSetDevice(ctx->device);
+  cudaError_t e = ax::launch_dequant(bits, packed, scale, zero, out, rows, k, packed_stride, out_stride,
+                                     ctx->num_sms, static_cast<cudaStream_t>(stream));
+  if (prev != ctx->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "weight decode");
+  ctx->last_error.clear();
+  return ANIMAXS_OK;
+}
+
 extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void* x,
                                     const void* w, void* out, void* stream) {
   if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
@@ -133,9 +184,31 @@ extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_de
   } restore{ctx->device, prev};
 
   const bool f32_out = d->epilogue == ANIMAXS_PROJ_GATE_ADD;
+  const bool rope = d->epilogue == ANIMAXS_PROJ_QKV_NORM && d->qk_norm == ANIMAXS_QK_RMS_ROPE;
+  const bool quant = d->w_storage != ANIMAXS_WEIGHT_FP16;
+  // Context scratch: the pair-major RoPE table, then the decoded fp16 weight.
+  const size_t rope_bytes = rope ? (static_cast<size_t>(d->tokens) * 64 * 8 + 255) / 256 * 256 : 0;
+  const size_t wdec_bytes = quant ? static_cast<size_t>(d->n) * d->k * 2 : 0;
+  if (rope || quant) {
+    rc = ax_ensure_scratch(ctx, rope_bytes + wdec_bytes);
+    if (rc != ANIMAXS_OK) return rc;
+  }
+  const void* wmat = w;
+  int64_t wstride = d->w_stride;
+  if (quant) {
+    // Decode the W8/W4 weight into fp16 (ordered before the GEMM on the same
+    // stream), as the reference's dequantize-then-GEMM path.
+    void* wdec = static_cast<char*>(ctx->scratch) + rope_bytes;
+    cudaError_t e = ax::launch_dequant(d->w_storage == ANIMAXS_WEIGHT_W4 ? 4 : 8, w, d->w_scale, d->w_zero, wdec,
+                                       d->n, d->k, d->w_packed_stride, d->k, ctx->num_sms,
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "weight decode");
+    wmat = wdec;
+    wstride = d->k;
+  }
   CUtensorMap ta, tb, tout;
   rc = make_tmap_2d(ctx, &ta, x, false, d->k, d->m, d->x_stride, 64, 128);
-  if (rc == ANIMAXS_OK) rc = make_tmap_2d(ctx, &tb, w, false, d->k, d->n, d->w_stride, 64, 128);
+  if (rc == ANIMAXS_OK) rc = make_tmap_2d(ctx, &tb, wmat, false, d->k, d->n, wstride, 64, 128);
   if (rc == ANIMAXS_OK)
     rc = f32_out ? make_tmap_2d(ctx, &tout, out, true, d->n, d->m, d->out_stride, 32, 128)
                  : make_tmap_2d(ctx, &tout, out, false, d->n, d->m, d->out_stride, 64, 128);
@@ -154,11 +227,9 @@ extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_de
   p.q_w = static_cast<const __half*>(d->q_norm_weight);
   p.k_w = static_cast<const __half*>(d->k_norm_weight);
   p.rope = nullptr;
-  if (d->epilogue == ANIMAXS_PROJ_QKV_NORM && d->qk_norm == ANIMAXS_QK_RMS_ROPE) {
+  if (rope) {
     // The epilogue reads the table pair-major: re-lay the `tokens` rows it uses
     // out into context scratch (ordered before the GEMM on the same stream).
-    rc = ax_ensure_scratch(ctx, static_cast<size_t>(d->tokens) * 64 * 8);
-    if (rc != ANIMAXS_OK) return rc;
     cudaError_t e = ax::launch_rope_pairs(d->rope_table, ctx->scratch, d->tokens, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "rope table re-layout");
     p.rope = static_cast<const float*>(ctx->scratch);

@@ -271,6 +271,16 @@ typedef enum animaxs_proj_epilogue {
                                 (gate_add_half_f32; `out` is the residual) */
 } animaxs_proj_epilogue;
 
+/* Weight storage of a projection (the reference's QuantizedLinearWeightBuffers,
+ * LinearExecutor.swift:12-40 and :460-520): fp16, or W8 / W4 codes with a
+ * per-row, per-64-column fp16 scale and zero, decoded as
+ * half(float(q) * float(scale) + float(zero)) (AnimaKernels.metal:19-67). */
+typedef enum animaxs_weight_storage {
+  ANIMAXS_WEIGHT_FP16 = 0,
+  ANIMAXS_WEIGHT_W8 = 1,  /* one byte per value */
+  ANIMAXS_WEIGHT_W4 = 2   /* two values per byte, even column in the low nibble */
+} animaxs_weight_storage;
+
 typedef struct animaxs_proj_desc {
   int32_t m;                 /* rows = images x tokens (`inputRows:`) */
   int32_t n;                 /* output features (rows of w) */
@@ -288,12 +298,18 @@ typedef struct animaxs_proj_desc {
   const void* k_norm_weight; /* DEVICE fp16[128], or NULL for ones */
   const float* rope_table;   /* DEVICE fp32[rope_rows][64][2][2] blocks [cos,-sin,sin,cos] */
   float eps;                 /* RMSNorm epsilon; 0 means 1e-6 */
-  int32_t reserved0;
+  int32_t w_storage;         /* animaxs_weight_storage of `w` */
   const float* gate;         /* GATE_ADD: DEVICE fp32 [m / tokens][gate_stride] */
   int64_t gate_stride;       /* elements between images' gate rows (>= n) */
+  const void* w_scale;       /* W8/W4: DEVICE fp16 [n][ceil(k / 64)] */
+  const void* w_zero;        /* W8/W4: DEVICE fp16 [n][ceil(k / 64)] */
+  int64_t w_packed_stride;   /* W8/W4: bytes between packed rows of `w` (>= k or ceil(k / 2)) */
 } animaxs_proj_desc;
 
-/* Dense defaults: strides = k / k / n, tokens = m, eps 1e-6. */
+/* Dense defaults: fp16 weights, strides = k / k / n, tokens = m, eps 1e-6.
+ * With W8/W4 weights the call first decodes them into context scratch
+ * (n * k * 2 bytes, as the reference's dequantized-MPS path), then runs the
+ * same GEMM. */
 int animaxs_proj_desc_init(animaxs_proj_desc* desc, int m, int n, int k, int epilogue);
 /* Validate exactly as animaxs_proj_forward does, without a GPU. */
 int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, const void* x,
@@ -302,6 +318,15 @@ int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, 
  * the attention kernel, while animaxs_attn_set_kernel_timing is on). */
 int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_desc* desc, const void* x,
                          const void* w, void* out, void* stream);
+
+/* Decode W8 (bits 8) or W4 (bits 4) codes `packed` [rows][packed_stride bytes]
+ * with fp16 `scale` / `zero` [rows][ceil(k / 64)] into fp16 `out`
+ * [rows][out_stride elements]: out = half(float(q) * float(scale) + float(zero)),
+ * rounded once after the multiply and once after the add.  Replaces
+ * dequant_w8_to_half / dequant_w4_to_half (AnimaKernels.metal:19-67). */
+int animaxs_dequant_to_half(animaxs_attn_ctx* ctx, int bits, const void* packed, const void* scale,
+                            const void* zero, void* out, int rows, int k, int64_t packed_stride,
+                            int64_t out_stride, void* stream);
 
 /* ---- Multi-GPU: heads sharded across ranks + one NCCL all-gather ----------
  * No counterpart exists in the reference (a single-device app); this serves

@@ -28,6 +28,10 @@ AnimaXS project):
                             path of ``attention_pytorch``)
 * masks ................... ``scripts/qwen_comfy_oracle.py:238-248``: additive
                             ``finfo.min / 4`` for causal (``triu(1)``) and key padding
+* W4/W8 weight decode ..... ``scripts/animapk_cuda/quant.py:32-76``
+                            (``decode_w4_matrix`` / ``decode_w8_matrix``),
+                            ``AnimaXS/Shaders/AnimaKernels.metal:19-67``
+                            (``dequant_w4_to_half`` / ``dequant_w8_to_half``)
 
 Parity is pinned: ``tests/golden/make_golden.py`` runs the reference's own
 functions (imported from the AnimaXS ``scripts/`` directory) on seeded inputs
@@ -309,3 +313,39 @@ def gate_add_projection(residual, x, w, gate, *, tokens: int) -> np.ndarray:
     g = np.asarray(gate, dtype=np.float32)
     rows = np.arange(branch.shape[0]) // tokens
     return (np.asarray(residual, dtype=np.float32) + branch * g[rows]).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Quantized (W4 / W8) projection weights
+# ---------------------------------------------------------------------------
+QUANT_GROUP = 64
+
+
+def dequant_to_half(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray, *, bits: int,
+                    k: int) -> np.ndarray:
+    """Decode W8 / W4 codes to fp16 (returned as float16).
+
+    ``packed`` is ``[rows][>= k]`` bytes (W8) or ``[rows][>= ceil(k / 2)]``
+    (W4: column ``2j`` in the low nibble of byte ``j``, ``2j + 1`` in the high
+    nibble); ``scale`` / ``zero`` are fp16 ``[rows][ceil(k / 64)]``, the groups of
+    64 columns restarting at every row.  value = ``q * scale + zero`` in fp32
+    (one rounding after the multiply, one after the add) then rounded to fp16:
+    scripts/animapk_cuda/quant.py:32-76 (``q * sg + zg``) and
+    AnimaKernels.metal:19-67 (``half(float(q) * float(sc) + float(ze))``).
+    """
+    packed = np.asarray(packed, dtype=np.uint8)
+    rows = packed.shape[0]
+    if bits == 4:
+        q = np.empty((rows, 2 * packed.shape[1]), dtype=np.uint8)
+        q[:, 0::2] = packed & 0x0F
+        q[:, 1::2] = packed >> 4
+        q = q[:, :k]
+    elif bits == 8:
+        q = packed[:, :k]
+    else:
+        raise ValueError("bits must be 4 or 8")
+    g = np.arange(k) // QUANT_GROUP
+    sc = np.asarray(scale, dtype=np.float16).astype(np.float32)[:, g]
+    ze = np.asarray(zero, dtype=np.float16).astype(np.float32)[:, g]
+    prod = (q.astype(np.float32) * sc).astype(np.float32)
+    return (prod + ze).astype(np.float32).astype(np.float16)

@@ -180,3 +180,29 @@ def proj_gate(seed: int, images: int = 2, tokens: int = 64, k: int = 256, n: int
     residual = torch.randn(images * tokens, n, generator=g).numpy()
     gate = (0.5 * torch.randn(images, n, generator=g)).numpy()
     return x, w, residual, gate
+
+
+def quant_weight(seed: int, rows: int, k: int, bits: int, packed_stride: int | None = None):
+    """Seeded W4 / W8 weight buffers in the reference's pack layout
+    (scripts/pack_anima.py:217-296): codes ``[rows][packed_stride]`` uint8 (W4:
+    two per byte, even column low), fp16 ``scale`` / ``zero`` ``[rows][ceil(k / 64)]``
+    with the magnitudes a quantized DiT weight has (span / qmax, group minimum)."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    need = (k + 1) // 2 if bits == 4 else k
+    stride = need if packed_stride is None else packed_stride
+    packed = torch.randint(0, 256, (rows, stride), generator=g, dtype=torch.int32).to(torch.uint8).numpy()
+    groups = (k + 63) // 64
+    qmax = 15.0 if bits == 4 else 255.0
+    span = torch.rand(rows, groups, generator=g) * 0.2 + 1e-3
+    lo = -span * torch.rand(rows, groups, generator=g)
+    scale = (span / qmax).to(torch.float16).numpy()
+    zero = lo.to(torch.float16).numpy()
+    return packed, scale, zero
+
+
+def proj_x(seed: int, rows: int, k: int) -> np.ndarray:
+    """Seeded fp16 activations ``[rows, k]`` for a projection."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    return torch.randn(rows, k, generator=g).half().numpy()

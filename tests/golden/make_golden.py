@@ -22,6 +22,13 @@ calls their functions -- ``rms_norm``, ``dit_rope``, ``apply_split_half_rope``,
 * ``proj_small.npz``    -- the fused projections (q|k|v with RMSNorm and
   RoPE, and the out-projection's gated residual) through ``linear``,
   ``rms_norm``, ``dit_rope`` and ``apply_split_half_rope``.
+* ``quant_small.npz``   -- W8 / W4 weights packed by the reference's own
+  quantizer (``scripts/pack_anima.py`` ``_quantize_chunk``, plain and with the
+  W4 range search) and decoded by its own decoders
+  (``scripts/animapk_cuda/quant.py`` ``decode_w8_matrix`` /
+  ``decode_w4_matrix``), with ragged groups and odd packed rows, plus one
+  projection through ``linear`` with the decoded W4 weight.  The packed bytes,
+  scales and zeros are stored verbatim: they are the kernels' inputs.
 
 Only the inputs' seeds are stored (plus checksums of the inputs to detect a
 change in ``torch.Generator``); tests regenerate inputs with
@@ -152,17 +159,51 @@ def make_proj(dso):
     np.savez_compressed(os.path.join(HERE, "proj_small.npz"), **out)
 
 
+def make_quant(dso, path):
+    """``quant_small.npz`` (see the module docstring)."""
+    sys.path.insert(0, os.path.join(path, "scripts"))
+    import pack_anima  # noqa: E402
+    from animapk_cuda import quant  # noqa: E402
+    out = {}
+    cases = [("w8", 8, 40, 200, False, 31), ("w4", 4, 40, 200, False, 32),
+             ("w4opt", 4, 33, 129, True, 33), ("w4wide", 4, 64, 1024, True, 34)]
+    for name, bits, rows, k, opt, seed in cases:
+        g = torch.Generator().manual_seed(seed)
+        chunk = (torch.randn(rows, k, generator=g) * 0.04).numpy().astype(np.float32)
+        chunk[0, 3] = 0.5                       # an outlier stretches one group's range
+        chunk[1, :64] = 0.125                   # a constant group (span < 1e-8: scale 1)
+        data, sc, ze, _ = pack_anima._quantize_chunk(chunk, bits, 64, opt)
+        dec = quant.decode_w4_matrix(data, sc, ze, rows, k) if bits == 4 else \
+            quant.decode_w8_matrix(data, sc, ze, rows, k)
+        groups = (k + 63) // 64
+        out[name + "_packed"] = np.frombuffer(data, dtype=np.uint8).reshape(rows, -1)
+        out[name + "_scale"] = np.frombuffer(sc, dtype="<f2").reshape(rows, groups)
+        out[name + "_zero"] = np.frombuffer(ze, dtype="<f2").reshape(rows, groups)
+        out[name + "_decoded_f32"] = dec.numpy().astype(np.float32)
+        out[name + "_decoded_half"] = dec.half().numpy()
+        out[name + "_meta"] = np.array([bits, rows, k, int(opt), seed], dtype=np.int64)
+    # A projection with the decoded W4 weight (the dequantize-then-GEMM path of
+    # LinearExecutor.swift:153-189) through the reference's linear.
+    x = torch.from_numpy(inputs.proj_x(35, 64, 1024))
+    wdec = torch.from_numpy(out["w4wide_decoded_half"])
+    out["proj_w4_out"] = dso.linear(x, wdec).float().numpy()
+    out["proj_w4_meta"] = np.array([35, 64, 1024], dtype=np.int64)
+    np.savez_compressed(os.path.join(HERE, "quant_small.npz"), **out)
+
+
 def main():
     global REF
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="AnimaXS source checkout")
     ap.add_argument("--skip-large", action="store_true")
-    ap.add_argument("--only-proj", action="store_true", help="write proj_small.npz only")
+    ap.add_argument("--only-proj", action="store_true",
+                    help="write proj_small.npz and quant_small.npz only")
     args = ap.parse_args()
     REF = load_reference(args.reference)
     dso, qco = REF
     torch.set_num_threads(os.cpu_count())
     make_proj(dso)
+    make_quant(dso, args.reference)
     if args.only_proj:
         return
 

@@ -213,6 +213,30 @@ def test_projection_validation(lib):
     assert _pvalidate(lib, _pdesc(lib, epilogue=2, n=256, out_stride=258)) == -1  # fp32 rows: 16 B
 
 
+def test_projection_quantized_weight_validation(lib):
+    """W8/W4 weight storage: scale/zero present and 2-byte aligned, packed rows
+    wide enough (ceil(k / 2) bytes for W4, k for W8); the packed codes need no
+    16-byte alignment (they are decoded into an aligned copy first)."""
+    from animaxs_b200._lib import WEIGHT_W4, WEIGHT_W8
+    q = dict(w_scale=0x7000, w_zero=0x8000)
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W4, w_packed_stride=128, **q)) == 0
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W8, w_packed_stride=256, **q)) == 0
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W4, w_packed_stride=128, **q),
+                      (0x1000, 0x2003, 0x3000)) == 0                    # byte-aligned codes
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W4, w_packed_stride=127, **q)) == -1
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W8, w_packed_stride=128, **q)) == -1
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W4, w_packed_stride=128, w_scale=0x7000)) == -1
+    assert _pvalidate(lib, _pdesc(lib, w_storage=WEIGHT_W4, w_packed_stride=128, w_scale=0x7001,
+                                  w_zero=0x8000)) == -1
+    assert _pvalidate(lib, _pdesc(lib, w_storage=3, w_packed_stride=256, **q)) == -1
+    assert _pvalidate(lib, _pdesc(lib), (0x1000, 0x2003, 0x3000)) == -1   # fp16 weight: 16 B
+
+
+def test_dequant_requires_context(lib):
+    """animaxs_dequant_to_half refuses a null context before touching a device."""
+    assert lib.animaxs_dequant_to_half(None, 4, 0x1000, 0x2000, 0x3000, 0x4000, 4, 64, 32, 64, None) == -1
+
+
 def test_selftest_rejects_bad_timeout(lib):
     """The failure-detection self-test validates its limit before touching a device."""
     assert lib.animaxs_attn_selftest_wait_timeout(None, 1000, None) == -1

@@ -171,3 +171,38 @@ def test_projection_oracle_matches_reference():
                                g["gate_in_checksum"], rtol=1e-12)
     got = ora.gate_add_projection(res, xg, wg, gate, tokens=tokens)
     np.testing.assert_allclose(got, g["gate_out"], atol=2e-5, rtol=1e-5)
+
+
+def test_quant_decode_oracle_matches_reference():
+    """dequant_to_half against the reference's own W8/W4 decoders on weights
+    packed by its own quantizer (tests/golden/quant_small.npz): bit-exact fp16,
+    and equal to the reference's fp32 reconstruction before the fp16 rounding;
+    then a projection through the decoded W4 weight against the reference's
+    linear (fp16 output, one fp16 ulp for the fp32 summation order)."""
+    g = _npz("quant_small.npz")
+    for name in ("w8", "w4", "w4opt", "w4wide"):
+        bits, rows, k, _opt, _seed = (int(v) for v in g[name + "_meta"])
+        got = ora.dequant_to_half(g[name + "_packed"], g[name + "_scale"], g[name + "_zero"], bits=bits, k=k)
+        assert got.shape == (rows, k)
+        assert np.array_equal(got.view(np.uint16), g[name + "_decoded_half"].view(np.uint16)), name
+        assert np.array_equal(got, g[name + "_decoded_f32"].astype(np.float16)), name
+    seed, m, k = (int(v) for v in g["proj_w4_meta"])
+    y = ora.linear_fp16(inputs.proj_x(seed, m, k), g["w4wide_decoded_half"])
+    np.testing.assert_allclose(y, g["proj_w4_out"], atol=2e-3, rtol=2e-3)
+
+
+def test_quant_decode_oracle_layout():
+    """Nibble order and group restart, on hand-made codes: byte 0x21 holds
+    column 0 = 1 (low nibble) and column 1 = 2; column 64 uses the second
+    group's scale and zero."""
+    packed = np.zeros((1, 33), dtype=np.uint8)
+    packed[0, 0] = 0x21
+    packed[0, 32] = 0x03
+    scale = np.array([[1.0, 0.5]], dtype=np.float16)
+    zero = np.array([[0.0, 10.0]], dtype=np.float16)
+    out = ora.dequant_to_half(packed, scale, zero, bits=4, k=65)
+    assert out[0, 0] == 1 and out[0, 1] == 2 and out[0, 2] == 0
+    assert out[0, 64] == np.float16(11.5)
+    w8 = ora.dequant_to_half(np.array([[255, 7]], dtype=np.uint8), np.array([[0.25]], dtype=np.float16),
+                             np.array([[-1.0]], dtype=np.float16), bits=8, k=2)
+    assert w8[0, 0] == np.float16(62.75) and w8[0, 1] == np.float16(0.75)
