@@ -581,9 +581,14 @@ def run_proj(args, rank, world, local_rank):
     g = torch.Generator(device=device).manual_seed(2024 + rank)
     m = BATCH * S_SELF
     xs = [torch.randn(m, D_MODEL, generator=g, device=device).half() for _ in range(POOL_BLOCKS)]
-    w_qkv = (torch.randn(3 * D_MODEL, D_MODEL, generator=g, device=device) / D_MODEL ** 0.5).half()
-    w_so, w_cq, w_co = ((torch.randn(D_MODEL, D_MODEL, generator=g, device=device) / D_MODEL ** 0.5).half()
-                        for _ in range(3))
+    bits = {"fp16": 16, "w8": 8, "w4": 4}[args.weights]
+
+    def make_w(rows):
+        w = (torch.randn(rows, D_MODEL, generator=g, device=device) / D_MODEL ** 0.5).half()
+        return w if bits == 16 else quantize_groups(w, bits)
+
+    w_qkv = make_w(3 * D_MODEL)
+    w_so, w_cq, w_co = (make_w(D_MODEL) for _ in range(3))
     qw = (1 + 0.1 * torch.randn(HD, generator=g, device=device)).half()
     kw = (1 + 0.1 * torch.randn(HD, generator=g, device=device)).half()
     rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).to(device)
@@ -634,6 +639,7 @@ def run_proj(args, rank, world, local_rank):
         t = torch.tensor([el], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         el = float(t.item())
+    decode = decode_roofline(pj, bits, device, stream) if bits != 16 else None
     if rank != 0:
         return
     peak_burst, peak_sust, _, peak_kind = peaks()
@@ -649,6 +655,8 @@ def run_proj(args, rank, world, local_rank):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic, random-init weights",
         "config": {"workload": "proj: 224 blocks x batch 8, x [32768, 2048] -> q|k|v [32768, 6144] and 3 x "
                                "[32768, 2048] projections", "parallelism": f"batch-shard x{world}",
+                   "weights": args.weights if bits == 16 else
+                   f"{args.weights}: group-64 codes decoded to fp16 on every call, then the GEMM",
                    "l2": f"x cycled over {POOL_BLOCKS} x 128 MiB (> 126 MB L2)"},
         "tflops_per_gpu": flops / (el / 1e3) / 1e12,
         "roofline": {"kernel": "proj_sm100_kernel (CTA-pair tcgen05 GEMM, fused epilogues; mean of the 4 "
@@ -658,10 +666,72 @@ def run_proj(args, rank, world, local_rank):
                      "frac_of_burst_peak": achieved / peak_burst, "avg_launch_ms": avg_kern,
                      "max_launch_ms": kern_max_ms, "launches_timed": n_kern, "traffic": None},
         "clocks": clocks,
-        "gpu_launches": args.steps * CALLS_PER_IMAGE * 5,   # 4 GEMMs + the RoPE-table re-layout
+        # 4 GEMMs + the RoPE-table re-layout (+ 4 weight decodes)
+        "gpu_launches": args.steps * CALLS_PER_IMAGE * (5 if bits == 16 else 9),
         "e2e": None,
     }
+    if decode is not None:
+        line["decode_roofline"] = decode
     print(json.dumps(line), flush=True)
+
+
+def quantize_groups(w, bits):
+    """Group-64 affine codes of an fp16 [n, k] weight on the device (the
+    reference packer's plain range, scripts/pack_anima.py:217-262): scale =
+    (max - min) / qmax, zero = min, q = rint((w - zero) / scale)."""
+    import torch
+
+    import animaxs_b200 as ax
+    n, k = w.shape
+    qmax = 15.0 if bits == 4 else 255.0
+    grp = w.float().view(n, k // 64, 64)
+    lo = grp.amin(dim=2)
+    span = grp.amax(dim=2) - lo
+    scale = torch.where(span >= 1e-8, span / qmax, torch.ones_like(span)).half()
+    zero = lo.half()
+    q = torch.clamp(torch.round((grp - zero.float()[..., None]) / scale.float()[..., None]), 0, qmax)
+    q = q.to(torch.uint8).view(n, k)
+    packed = (q[:, 0::2] | (q[:, 1::2] << 4)).contiguous() if bits == 4 else q.contiguous()
+    return ax.QuantizedWeight(packed, scale.contiguous(), zero.contiguous(), bits, k)
+
+
+def decode_roofline(pj, bits, device, stream, pool=6, reps=5):
+    """The weight decode alone (dequant_kernel): the DiT q|k|v weight shape
+    [6144, 2048], cycled over `pool` weights whose fp16 outputs total > L2.
+    Algorithmic bytes per launch = codes + scale + zero read + fp16 written."""
+    import torch
+    n, k = 3 * D_MODEL, D_MODEL
+    g = torch.Generator(device=device).manual_seed(77)
+    ws = [quantize_groups(torch.randn(n, k, generator=g, device=device).half(), bits) for _ in range(pool)]
+    outs = [torch.empty(n, k, dtype=torch.float16, device=device) for _ in range(pool)]
+    for w, o in zip(ws, outs):
+        pj.dequant(w, o, stream=stream)
+    torch.cuda.synchronize(device)
+    # The launches are replayed from a CUDA graph so that the events time the
+    # kernels back to back, not the host's per-call overhead.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            for w, o in zip(ws, outs):
+                pj.dequant(w, o)
+    graph.replay()
+    torch.cuda.synchronize(device)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    per_launch_ms = t0.elapsed_time(t1) / (reps * pool)
+    del graph
+    nbytes = n * k * bits // 8 + 2 * n * (k // 64) * 2 + n * k * 2
+    hbm = peaks()[2]
+    achieved = nbytes / (per_launch_ms / 1e3) / 1e9
+    return {"kernel": f"dequant_kernel<{bits}> ([6144, 2048] weight, {pool} weights cycled, "
+                      f"{pool * n * k * 2 / 2**20:.0f} MiB of fp16 outputs > L2, {reps * pool} launches "
+                      "replayed from a CUDA graph)",
+            "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+            "bytes_per_launch": nbytes, "avg_launch_ms": per_launch_ms}
 
 
 def profile_kernel(args):
@@ -676,6 +746,8 @@ def profile_kernel(args):
         m = 4 * S_SELF
         x = torch.randn(m, D_MODEL, generator=g, device="cuda").half()
         w = (torch.randn(3 * D_MODEL, D_MODEL, generator=g, device="cuda") / D_MODEL ** 0.5).half()
+        if args.weights != "fp16":   # each call then decodes the weight (dequant_kernel) first
+            w = quantize_groups(w, 4 if args.weights == "w4" else 8)
         out = torch.empty(m, 3 * D_MODEL, dtype=torch.float16, device="cuda")
         nw = torch.ones(HD, dtype=torch.float16, device="cuda")
         rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64).reshape(S_SELF, 64, 2, 2)).cuda()
@@ -720,6 +792,8 @@ def main():
     ap.add_argument("--impl", default="animaxs", choices=["animaxs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--weights", default="fp16", choices=["fp16", "w8", "w4"],
+                    help="projection weight storage for --workload proj")
     ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae", "proj"],
                     help="cfg4 (default): the 8-step DiT workload, batch-sharded; cfg5: the "
                          "16384-token self-attention, heads sharded + one NCCL all-gather; vae: "
