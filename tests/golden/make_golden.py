@@ -22,6 +22,12 @@ calls their functions -- ``rms_norm``, ``dit_rope``, ``apply_split_half_rope``,
 * ``proj_small.npz``    -- the fused projections (q|k|v with RMSNorm and
   RoPE, and the out-projection's gated residual) through ``linear``,
   ``rms_norm``, ``dit_rope`` and ``apply_split_half_rope``.
+* ``real_context.npz``  -- real activations from the reference's committed
+  ``scripts/oracle_out/adapter_oracle_case1.npz`` (an actual prompt run
+  through the model): the LLM adapter's block-0 hidden state [47, 1024]
+  (magnitudes up to 64) and the 47 valid rows of the 512-row padded context
+  the DiT cross-attention reads, stored as fp16.  Used as realistic attention
+  inputs (heavy-tailed values, a context padded with zero rows).
 * ``quant_small.npz``   -- W8 / W4 weights packed by the reference's own
   quantizer (``scripts/pack_anima.py`` ``_quantize_chunk``, plain and with the
   W4 range search) and decoded by its own decoders
@@ -191,19 +197,35 @@ def make_quant(dso, path):
     np.savez_compressed(os.path.join(HERE, "quant_small.npz"), **out)
 
 
+def make_real_context(path):
+    """``real_context.npz`` (see the module docstring)."""
+    z = np.load(os.path.join(path, "scripts/oracle_out/adapter_oracle_case1.npz"))
+    ctx = z["adapter_out_padded512"][0]
+    valid = int((np.abs(ctx).sum(axis=1) > 0).sum())
+    assert not np.abs(ctx[valid:]).any(), "padding rows are expected to be zero"
+    out = {
+        "hidden": z["adapter_block_00"][0].astype(np.float16),
+        "context_valid": ctx[:valid].astype(np.float16),
+        "context_rows": np.array([ctx.shape[0], valid], dtype=np.int64),
+        "source_commit": np.array(str(z["commit"])),
+    }
+    np.savez_compressed(os.path.join(HERE, "real_context.npz"), **out)
+
+
 def main():
     global REF
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="AnimaXS source checkout")
     ap.add_argument("--skip-large", action="store_true")
     ap.add_argument("--only-proj", action="store_true",
-                    help="write proj_small.npz and quant_small.npz only")
+                    help="write proj_small.npz, quant_small.npz and real_context.npz only")
     args = ap.parse_args()
     REF = load_reference(args.reference)
     dso, qco = REF
     torch.set_num_threads(os.cpu_count())
     make_proj(dso)
     make_quant(dso, args.reference)
+    make_real_context(args.reference)
     if args.only_proj:
         return
 
