@@ -117,6 +117,11 @@ SIGNATURES = {
     "animaxs_comm_create": (_I, [_P, _I, _I, _P, ctypes.POINTER(_P)]),
     "animaxs_comm_destroy": (_I, [_P]),
     "animaxs_attn_forward_head_sharded": (_I, [_P, _P, _DESC, _P, _P, _P, _P, _P]),
+    "animaxs_peer_group_create": (_I, [_P, _I, _I, _I64, ctypes.POINTER(_P), _P]),
+    "animaxs_peer_group_connect": (_I, [_P, _P]),
+    "animaxs_peer_group_output": (_P, [_P]),
+    "animaxs_peer_group_destroy": (_I, [_P]),
+    "animaxs_attn_forward_head_sharded_peer": (_I, [_P, _P, _DESC, _P, _P, _P, _P, _P]),
     "animaxs_attn_forward_noalloc": (_I, [_DESC, _P, _P, _P, _P, _P]),
     "animaxs_attn_selftest_wait_timeout": (_I, [_P, _I64, _P]),
     "animaxs_proj_desc_init": (_I, [ctypes.POINTER(ProjDesc), _I, _I, _I, _I]),

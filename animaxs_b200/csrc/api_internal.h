@@ -40,6 +40,13 @@ int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q
                 const void* v, const void* o);
 int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int64_t dim, int64_t rows,
                  int64_t heads, int64_t batch, int64_t st, int64_t sh, int64_t sb, int box_rows = 128);
+// Peers of a fused head-sharded call: the epilogue stores every output tile
+// also at o + delta[i] and the CTAs count their items on arrive[i].
+struct AxPeers {
+  int n;
+  long long delta[7];
+  unsigned int* arrive[7];
+};
 int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q,
                      const void* k, const void* v, void* o, int heads_begin, int heads_count,
-                     const AxOutView* o_view, cudaStream_t stream);
+                     const AxOutView* o_view, cudaStream_t stream, const AxPeers* peers = nullptr);

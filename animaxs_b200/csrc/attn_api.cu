@@ -306,7 +306,7 @@ extern "C" int animaxs_attn_scratch_bytes(const animaxs_attn_desc* d, int64_t* b
 // caller redirect the output.
 int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q,
                      const void* k, const void* v, void* o, int heads_begin, int heads_count,
-                     const AxOutView* o_view, cudaStream_t stream) {
+                     const AxOutView* o_view, cudaStream_t stream, const AxPeers* peers) {
   int prev = 0;
   cudaGetDevice(&prev);
   if (prev != ctx->device) cudaSetDevice(ctx->device);
@@ -427,6 +427,15 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     p.o_batch = d->o_batch_stride;
   }
   p.status = ctx->d_status;
+  if (peers != nullptr) {
+    if (peers->n < 0 || peers->n > ax::kMaxPeers || (d->head_dim != 64 && d->head_dim != 128))
+      return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "peer stores need head_dim 64 or 128 and <= 7 peers");
+    p.n_peers = peers->n;
+    for (int i = 0; i < peers->n; ++i) {
+      p.peer_delta[i] = peers->delta[i];
+      p.peer_arrive[i] = peers->arrive[i];
+    }
+  }
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
   if (ctx->timing) {
     while (ctx->events.size() < ctx->events_used + 2) {

@@ -39,6 +39,11 @@
 // execute in issue order, which is what lets QK_X(j+1) overwrite the TMEM
 // columns PV_X(j) reads P_X(j) from.  Barrier phases count tiles and items
 // across the whole persistent loop.
+//
+// Head-sharded calls over several GPUs (p.n_peers > 0) fuse the all-gather
+// into the epilogue: each staged output tile is also stored into every peer's
+// output over NVLink, and each CTA then adds its item count to every peer's
+// arrival word (release, system scope) for the peer's closing wait.
 #include <atomic>
 
 #include "api_internal.h"
@@ -490,6 +495,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                            I.q0 + X * kTileM + (warp & 3) * 32, I.h - p.o_head_base, I.b);
               tma_store_commit();
             }
+            if (p.n_peers > 0) {
+              // Fused head-sharded gather: the same 32 x 64 tile to the same
+              // place in every peer's output over NVLink, 8 lanes per row
+              // (128 contiguous bytes), 4 rows per step.  The stage is only
+              // read here; the next round rewrites it after the __syncwarp
+              // that follows lane 0's wait.
+              const uint32_t wstage = base + L::kStage + static_cast<uint32_t>(warp) * 4096u;
+              const int u = lane & 7;
+              const long long obase = static_cast<long long>(I.b) * p.o_batch +
+                                      static_cast<long long>(I.h - p.o_head_base) * p.o_head + 64 * rd + 8 * u;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int r = 4 * i + (lane >> 3);
+                const int grow = I.q0 + X * kTileM + (warp & 3) * 32 + r;
+                const uint4 val = ld_shared_v4u(wstage + r * 128u + ((u ^ (r & 7)) << 4));
+                if (grow < p.q_len) {
+                  char* dst = reinterpret_cast<char*>(p.o + obase + static_cast<long long>(grow) * p.o_tok);
+                  for (int pi = 0; pi < p.n_peers; ++pi)
+                    *reinterpret_cast<uint4*>(dst + p.peer_delta[pi]) = val;
+                }
+              }
+            }
           }
         }
         ++eX;
@@ -499,11 +526,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (warp < 8 && lane == 0) tma_store_wait_all();  // the output stores have completed
+  if (p.n_peers > 0 && warp < 8) __threadfence_system();  // peer stores before the arrival below
   tc_fence_before();
   __syncthreads();
   if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+  if (p.n_peers > 0 && threadIdx.x == 0 && *abort_flag == 0) {
+    // This CTA's items are in every peer's output: count them on each peer's
+    // arrival word for this rank (a CTA that timed out does not arrive, so the
+    // peers' waits report the failure instead of reading a partial output).
+    const int mine = static_cast<int>(blockIdx.x) < p.n_items
+                         ? (p.n_items - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                         : 0;
+    for (int pi = 0; pi < p.n_peers; ++pi) red_add_release_sys(p.peer_arrive[pi], static_cast<unsigned>(mine));
   }
 #undef BAR
 }

@@ -29,7 +29,17 @@ struct AttnFwdParams {
   __half* o;
   long long o_tok, o_head, o_batch;  // output strides (elements)
   unsigned int* status;  // device status word (bit 0: a bounded wait timed out)
+  // Fused head-sharded gather (head dims 64 / 128; n_peers = 0 otherwise): the
+  // epilogue also stores every output tile at the same offset in each peer's
+  // output (peer GPU memory mapped into this process), and each CTA that
+  // finished without a timeout adds its item count to every peer's arrival
+  // word for this rank.
+  int n_peers;
+  long long peer_delta[7];           // bytes from `o` to the peer's copy of it
+  unsigned int* peer_arrive[7];      // the peer's arrival word for this rank
 };
+
+constexpr int kMaxPeers = 7;  // 8 GPUs per node
 
 constexpr unsigned int kStatusTimeoutBit = 1u;  // a bounded device wait expired
 
@@ -70,6 +80,21 @@ cudaError_t launch_attn_wide(const CUtensorMap& tq, const CUtensorMap& tk, const
 int attn_fwd_rows_per_cta();  // query rows one attention CTA covers (head dims 64 / 128)
 
 cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
+
+// Peer handshake of the fused head-sharded path (peer_sync.cu): one block adds
+// `add` to each peer's word `signal[i]` (release, system scope), then waits
+// until every own word `wait[i]` (i != rank) has reached `target` (acquire,
+// system scope; bounded by timeout_ns, after which kStatusTimeoutBit is set).
+struct PeerSyncParams {
+  unsigned int* signal[8];   // peers' words for this rank (mapped here); nullptr: no signal
+  unsigned int add;
+  const unsigned int* wait;  // this rank's [world] words
+  unsigned int target;
+  int world, rank;
+  unsigned long long timeout_ns;
+  unsigned int* status;
+};
+cudaError_t launch_peer_sync(const PeerSyncParams& p, cudaStream_t stream);
 
 // Fused attention projections (proj_sm100.cu): out = x w^T over fp16 operands
 // with fp32 accumulation, then one of three epilogues.

@@ -1,4 +1,7 @@
-"""Heads sharded across GPUs + one NCCL all-gather (the 16K-token DiT case).
+"""Heads sharded across GPUs (the 16K-token DiT case): the rank's heads, then
+either one NCCL all-gather (:class:`HeadShardedAttention`) or, fused, the
+attention kernel storing every output tile into every rank's output over
+NVLink (:class:`PeerShardedAttention`).
 
 Each rank of a ``torch.distributed`` group computes query heads
 ``head_range(rank, world, heads)`` of the attention for every query row (each
@@ -87,3 +90,82 @@ class HeadShardedAttention:
             v.data_ptr(), out.data_ptr(), _stream_handle(stream))
         raise_for(rc, self.ex.last_error())
         return out
+
+
+class _DeviceArray:
+    """A CUDA array interface over memory the library owns (no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f2"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def exchange_handles(handle: bytes, group=None) -> bytes:
+    """Every rank's 64-byte IPC handle, concatenated in rank order."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    got = [None] * world
+    dist.all_gather_object(got, handle, group=group)
+    if any(not isinstance(h, (bytes, bytearray)) or len(h) != 64 for h in got):
+        raise AttentionValidationError(_lib.ERR_INVALID_ARG, "IPC handles must be 64 bytes")
+    return b"".join(bytes(h) for h in got)
+
+
+class PeerShardedAttention:
+    """Config-5 head-sharded attention with the all-gather fused into the
+    attention kernel: each rank's output buffer ([B, S, H, D] fp16, owned by
+    the library, shared over CUDA IPC) receives every rank's heads directly
+    from the kernels' epilogues (``animaxs_attn_forward_head_sharded_peer``).
+    ``torch.distributed`` only carries the IPC handles at setup.  Every rank
+    makes the same calls in the same order; ``output`` is valid until this
+    rank's next call."""
+
+    def __init__(self, executor, rank: int, world: int, out_shape, group=None, exchange=None):
+        import torch
+        self.ex = executor
+        self.rank, self.world = rank, world
+        self.shape = tuple(int(x) for x in out_shape)
+        nbytes = 2
+        for x in self.shape:
+            nbytes *= x
+        lib = _lib.lib()
+        grp = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        rc = lib.animaxs_peer_group_create(executor.handle, world, rank, nbytes, ctypes.byref(grp), handle)
+        raise_for(rc, executor.last_error())
+        self._group = grp
+        try:
+            allh = exchange(handle.raw) if exchange else exchange_handles(handle.raw, group)
+            rc = lib.animaxs_peer_group_connect(grp, ctypes.create_string_buffer(allh, len(allh)))
+            raise_for(rc, executor.last_error())
+        except Exception:
+            self.close()
+            raise
+        ptr = lib.animaxs_peer_group_output(grp)
+        self.output = torch.as_tensor(_DeviceArray(ptr, self.shape), device=f"cuda:{executor.device}")
+
+    def close(self):
+        if getattr(self, "_group", None):
+            self.output = None
+            _lib.lib().animaxs_peer_group_destroy(self._group)
+            self._group = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __call__(self, q, k, v, *, stream=None, **kw):
+        """Same arguments as AttentionExecutor.attention (q/k/v are the FULL
+        tensors); returns ``output``, which holds every rank's heads."""
+        import torch
+        from .executor import _stream_handle
+        desc = self.ex.strided_desc(q, k, v, self.output, **kw)
+        if stream is None:
+            stream = torch.cuda.current_stream(q.device)
+        rc = _lib.lib().animaxs_attn_forward_head_sharded_peer(
+            self.ex.handle, self._group, ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            self.output.data_ptr(), _stream_handle(stream))
+        raise_for(rc, self.ex.last_error())
+        return self.output

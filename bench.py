@@ -346,28 +346,42 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
 
 def run_cfg5(args, rank, world, local_rank):
     """Config 5: 16384-token DiT self-attention (rms + 3-D RoPE 1x128x128), 16
-    heads sharded over the ranks, one NCCL all-gather of the [16384, 2048] fp16
-    output; every rank ends with the full output.  value = calls/s."""
+    heads sharded over the ranks; every rank ends with the full [16384, 2048]
+    fp16 output.  The gather is fused into the attention kernel by default
+    (`--gather peer`: every rank's epilogue stores its tiles into every rank's
+    output over NVLink) or one NCCL all-gather (`--gather nccl`); one GPU
+    needs no gather.  value = calls/s."""
     import torch
     import torch.distributed as dist
 
     import animaxs_b200 as ax
-    from animaxs_b200.sharded import HeadShardedAttention, share_unique_id
+    from animaxs_b200.sharded import HeadShardedAttention, PeerShardedAttention, share_unique_id
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     ex = ax.AttentionExecutor(local_rank)
-    if world > 1:
-        uid = share_unique_id()
-    else:
-        from animaxs_b200.sharded import nccl_unique_id
-        uid = nccl_unique_id()
-    sh = HeadShardedAttention(ex, rank, world, uid)
     s_len = 16384
     g = torch.Generator(device=device).manual_seed(0)
     q, k, v = (torch.randn(1, s_len, HEADS, HD, generator=g, device=device).half() for _ in range(3))
     rope = torch.from_numpy(ax.DitRoPE.generate(1, 128, 128).reshape(s_len, 64, 2, 2)).to(device)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(device)
+    gather = args.gather if world > 1 else "none"
+    if gather == "nccl":
+        sh = HeadShardedAttention(ex, rank, world, share_unique_id())
+    elif gather == "peer":
+        sh = PeerShardedAttention(ex, rank, world, q.shape)
+    else:
+        class _Single:
+            def __call__(self, q, k, v, out=None, **kw):
+                return ex.attention(q, k, v, out=out, **kw)
+
+            def close(self):
+                pass
+        sh = _Single()
+    if gather == "peer":
+        call = lambda: sh(q, k, v, qk_norm="rms_rope", rope_table=rope, stream=stream)  # noqa: E731
+    else:
+        call = lambda: sh(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope, stream=stream)  # noqa: E731
 
     def barrier():
         if world > 1:
@@ -375,7 +389,7 @@ def run_cfg5(args, rank, world, local_rank):
         torch.cuda.synchronize(device)
 
     for _ in range(args.warmup):
-        sh(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope, stream=stream)
+        call()
     barrier()
     sampler = ClockSampler(local_rank)
     sampler.start()
@@ -385,7 +399,7 @@ def run_cfg5(args, rank, world, local_rank):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
-        sh(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope, stream=stream)
+        call()
     t1.record(stream)
     barrier()
     clocks = sampler.stop()
@@ -401,13 +415,16 @@ def run_cfg5(args, rank, world, local_rank):
         return
     peak_burst, peak_sust, _, peak_kind = peaks()
     tf = flops * args.steps / (el / 1e3) / 1e12
+    how = {"peer": "gather fused into the attention epilogue (NVLink stores)",
+           "nccl": "NCCL all-gather", "none": "one GPU, no gather"}[gather]
     print(json.dumps({
-        "metric": "config-5 DiT self-attention, 16384 tokens, heads sharded + NCCL all-gather",
+        "metric": "config-5 DiT self-attention, 16384 tokens, heads sharded, every rank ends with the "
+                  "full output",
         "value": args.steps / (el / 1e3), "unit": "calls/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": el / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": "config5: S=16384, 16 heads x 128, rms + rope3d(1,128,128)",
-                   "parallelism": f"heads/{world} + all-gather"},
+                   "parallelism": f"heads/{world}", "gather": how},
         "tflops_total": tf, "tflops_per_gpu": tf / world,
         "frac_of_sustained_peak_per_gpu": tf / world / peak_sust, "peak_kind": peak_kind,
         "clocks": clocks}), flush=True)
@@ -792,6 +809,8 @@ def main():
     ap.add_argument("--impl", default="animaxs", choices=["animaxs", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="config-5 gather across ranks: fused NVLink stores or NCCL all-gather")
     ap.add_argument("--weights", default="fp16", choices=["fp16", "w8", "w4"],
                     help="projection weight storage for --workload proj")
     ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae", "proj"],

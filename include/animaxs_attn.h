@@ -349,6 +349,33 @@ int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_comm* comm,
                                       const animaxs_attn_desc* desc, const void* q,
                                       const void* k, const void* v, void* o, void* stream);
 
+/* ---- Multi-GPU, fused: heads sharded, the gather done by the attention kernel
+ * Same split of the heads as animaxs_attn_forward_head_sharded, without NCCL:
+ * every rank's output buffer is mapped into every other rank's process (CUDA
+ * IPC over NVLink / NVSwitch), the attention kernel stores each finished output
+ * tile into every rank's buffer, and a one-block handshake before and after
+ * (bounded waits on system-scope flags) orders the calls.
+ *
+ * Setup, on every rank: animaxs_peer_group_create allocates this rank's output
+ * buffer (output_bytes, plus the flags) and returns its 64-byte IPC handle; the
+ * caller exchanges the handles (any side channel, rank order); then
+ * animaxs_peer_group_connect maps the peers' buffers.  Every call passes
+ * o = animaxs_peer_group_output(group) with the same descriptor on all ranks,
+ * in the same order (like a collective); the output stays valid until this
+ * rank's next call.  A peer that does not arrive within ANIMAXS_WAIT_TIMEOUT
+ * (2 s) makes animaxs_attn_synchronize report ANIMAXS_ERR_TIMEOUT; the group
+ * must then be destroyed and recreated. */
+typedef struct animaxs_peer_group animaxs_peer_group;
+
+int animaxs_peer_group_create(animaxs_attn_ctx* ctx, int world, int rank, int64_t output_bytes,
+                              animaxs_peer_group** out, void* ipc_handle64);
+int animaxs_peer_group_connect(animaxs_peer_group* group, const void* handles64 /* world x 64 B */);
+void* animaxs_peer_group_output(animaxs_peer_group* group);
+int animaxs_peer_group_destroy(animaxs_peer_group* group);
+int animaxs_attn_forward_head_sharded_peer(animaxs_attn_ctx* ctx, animaxs_peer_group* group,
+                                           const animaxs_attn_desc* desc, const void* q,
+                                           const void* k, const void* v, void* o, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -237,6 +237,18 @@ def test_dequant_requires_context(lib):
     assert lib.animaxs_dequant_to_half(None, 4, 0x1000, 0x2000, 0x3000, 0x4000, 4, 64, 32, 64, None) == -1
 
 
+def test_peer_group_rejects_bad_arguments(lib):
+    """The fused head-sharded entry points check their arguments before any
+    device call."""
+    grp = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    assert lib.animaxs_peer_group_create(None, 2, 0, 1024, ctypes.byref(grp), h) == -1
+    assert lib.animaxs_peer_group_connect(None, h) == -1
+    assert lib.animaxs_peer_group_output(None) is None
+    assert lib.animaxs_peer_group_destroy(None) == 0
+    assert lib.animaxs_attn_forward_head_sharded_peer(None, None, None, 0, 0, 0, 0, None) == -1
+
+
 def test_selftest_rejects_bad_timeout(lib):
     """The failure-detection self-test validates its limit before touching a device."""
     assert lib.animaxs_attn_selftest_wait_timeout(None, 1000, None) == -1

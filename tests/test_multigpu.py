@@ -1,11 +1,20 @@
 """Multi-GPU paths.
 
-CPU part (gloo, world size 2, runs everywhere): the head partition and the
-sharing of the NCCL id across ranks.  GPU part (2 GPUs, skipped otherwise):
-heads sharded over two ranks + the library's NCCL all-gather must reproduce
-the single-GPU result, and a rank that never joins must make the other rank's
-communicator creation fail with ANIMAXS_ERR_TIMEOUT instead of hanging.
-Failures are made on the host only; NVLS is off in these children.
+CPU part (gloo, world size 2, runs everywhere):
+* the head partition;
+* the sharing of the NCCL id and of the IPC handles across ranks.
+
+GPU part (2 GPUs, skipped otherwise):
+* Heads sharded over two ranks must reproduce the single-GPU result bit for
+  bit, both with the library's NCCL all-gather and with the fused peer path,
+  where the attention kernel stores every tile into both ranks' outputs over
+  NVLink.
+* A rank that never joins must make the other rank fail with
+  ANIMAXS_ERR_TIMEOUT instead of hanging. For NCCL that is communicator
+  creation; for the peer path, the bounded handshake waits.
+
+Failures are made on the host only (a rank that does not call).  NVLS is off
+in these children and no kernel uses multimem.
 """
 import os
 import socket
@@ -50,6 +59,25 @@ def test_unique_id_is_shared_over_gloo():
     out = mgr.dict()
     mp.spawn(_gloo_uid_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     assert out[0] == out[1] == bytes(range(128))
+
+
+def _gloo_handles_worker(rank, world, port, out):
+    import torch.distributed as dist
+    from animaxs_b200.sharded import exchange_handles
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    out[rank] = exchange_handles(bytes([rank]) * 64)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ipc_handles_are_exchanged_in_rank_order_over_gloo():
+    import torch.multiprocessing as mp
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_gloo_handles_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    want = bytes([0]) * 64 + bytes([1]) * 64
+    assert out[0] == out[1] == want
 
 
 # ------------------------------------------------------------------ 2 GPUs --
@@ -145,6 +173,97 @@ def test_rank_that_never_joins_times_out():
     out = mgr.dict()
     mp.spawn(_absent_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     assert out[0] == "timeout"
+
+
+def _peer_worker(rank, world, port, out):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import torch.distributed as dist
+
+    import animaxs_b200 as ax
+    from animaxs_b200.sharded import PeerShardedAttention
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    ex = ax.AttentionExecutor(rank)
+    s_len = 2048
+    ps = PeerShardedAttention(ex, rank, world, (1, s_len, 16, 128))
+    g = torch.Generator(device="cuda").manual_seed(5)   # the same inputs on both ranks
+    rope = torch.from_numpy(ax.DitRoPE.generate(1, 32, 64)).cuda()
+    errs = []
+    for call in range(3):   # repeated calls: the handshake words advance per call
+        q, k, v = (torch.randn(1, s_len, 16, 128, generator=g, device="cuda").half() for _ in range(3))
+        got = ps(q, k, v, qk_norm="rms_rope", rope_table=rope) if call != 1 else ps(q, k, v)
+        ex.synchronize()
+        ref = ex.attention(q, k, v, qk_norm="rms_rope", rope_table=rope) if call != 1 else ex.attention(q, k, v)
+        torch.cuda.synchronize()
+        errs.append(float((got.float() - ref.float()).abs().max()))
+        dist.barrier()   # the next call may overwrite the output
+    out[rank] = errs
+    ps.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.timeout(180)
+@needs2
+def test_peer_fused_head_sharded_matches_single_gpu():
+    """The attention kernel stores its heads into both ranks' outputs (NVLink);
+    every rank's buffer equals the single-GPU result bit for bit."""
+    import torch.multiprocessing as mp
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    for rank in (0, 1):
+        assert out[rank] == [0.0, 0.0, 0.0], f"rank {rank}: max differences {out[rank]}"
+
+
+def _peer_absent_worker(rank, world, port, out):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import torch.distributed as dist
+
+    import animaxs_b200 as ax
+    from animaxs_b200 import AttentionTimeoutError
+    from animaxs_b200.sharded import PeerShardedAttention
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    ex = ax.AttentionExecutor(rank)
+    ps = PeerShardedAttention(ex, rank, world, (1, 512, 16, 128))
+    if rank == 0:
+        # Rank 1 stays alive but never calls: both bounded waits of this call
+        # give up (2 s each) and the status word reports the timeout.
+        g = torch.Generator(device="cuda").manual_seed(1)
+        q, k, v = (torch.randn(1, 512, 16, 128, generator=g, device="cuda").half() for _ in range(3))
+        ps(q, k, v)
+        try:
+            ex.synchronize()
+            out[0] = "completed"
+        except AttentionTimeoutError:
+            out[0] = "timeout"
+        # the context still works after the report
+        ref = ex.attention(q, k, v)
+        ex.synchronize()
+        out["after"] = bool(torch.isfinite(ref.float()).all())
+    dist.barrier()   # rank 1 leaves only after rank 0's kernels have finished
+    ps.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.timeout(180)
+@needs2
+def test_peer_that_never_calls_times_out():
+    import torch.multiprocessing as mp
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_peer_absent_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    assert out[0] == "timeout" and out["after"]
 
 
 def test_config4_prompt_seeds_are_disjoint_across_ranks():
