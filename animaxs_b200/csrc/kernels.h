@@ -10,7 +10,8 @@ namespace ax {
 
 // Parameters of the flash-attention kernels (attn_fwd_sm100.cu, attn_wide_sm100.cu).  q/k/v arrive
 // through TMA tensor maps over [batch][head][token][head_dim] fp16 views (any
-// strides); the output is written with plain stores.
+// strides); the output leaves through TMA tensor stores from a shared-memory
+// stage (the launchers build its tensor map from `o` and the strides below).
 struct AttnFwdParams {
   int head_dim;          // 64 or 128 (attn_fwd_sm100.cu), 256 or 384 (attn_wide_sm100.cu)
   int q_len;
