@@ -120,11 +120,17 @@ class PeerShardedAttention:
     makes the same calls in the same order; ``output`` is valid until this
     rank's next call."""
 
-    def __init__(self, executor, rank: int, world: int, out_shape, group=None, exchange=None):
+    def __init__(self, executor, rank: int, world: int, out_shape, group=None, exchange=None,
+                 layout: str = "token"):
+        """``out_shape`` is ``[B, S, H, D]``; ``layout`` "token" stores it
+        token-major (``[B, S, H, D]`` contiguous), "head" head-major
+        (``[B, H, S, D]`` contiguous, ``output`` is the ``[B, S, H, D]`` view)."""
         import torch
         self.ex = executor
         self.rank, self.world = rank, world
         self.shape = tuple(int(x) for x in out_shape)
+        if len(self.shape) != 4 or layout not in ("token", "head"):
+            raise AttentionValidationError(_lib.ERR_INVALID_ARG, "out_shape [B, S, H, D]; layout token or head")
         nbytes = 2
         for x in self.shape:
             nbytes *= x
@@ -142,7 +148,12 @@ class PeerShardedAttention:
             self.close()
             raise
         ptr = lib.animaxs_peer_group_output(grp)
-        self.output = torch.as_tensor(_DeviceArray(ptr, self.shape), device=f"cuda:{executor.device}")
+        b, sq, h, d = self.shape
+        dev = f"cuda:{executor.device}"
+        if layout == "head":
+            self.output = torch.as_tensor(_DeviceArray(ptr, (b, h, sq, d)), device=dev).permute(0, 2, 1, 3)
+        else:
+            self.output = torch.as_tensor(_DeviceArray(ptr, self.shape), device=dev)
 
     def close(self):
         if getattr(self, "_group", None):

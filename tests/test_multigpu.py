@@ -55,7 +55,7 @@ def _gloo_uid_worker(rank, world, port, out):
 
 def test_unique_id_is_shared_over_gloo():
     import torch.multiprocessing as mp
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_gloo_uid_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     assert out[0] == out[1] == bytes(range(128))
@@ -73,7 +73,7 @@ def _gloo_handles_worker(rank, world, port, out):
 
 def test_ipc_handles_are_exchanged_in_rank_order_over_gloo():
     import torch.multiprocessing as mp
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_gloo_handles_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     want = bytes([0]) * 64 + bytes([1]) * 64
@@ -130,7 +130,7 @@ def _sharded_worker(rank, world, port, out):
 @needs2
 def test_head_sharded_matches_single_gpu():
     import torch.multiprocessing as mp
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_sharded_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     for rank in (0, 1):
@@ -169,7 +169,7 @@ def _absent_peer_worker(rank, world, port, out):
 @needs2
 def test_rank_that_never_joins_times_out():
     import torch.multiprocessing as mp
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_absent_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     assert out[0] == "timeout"
@@ -199,8 +199,30 @@ def _peer_worker(rank, world, port, out):
         torch.cuda.synchronize()
         errs.append(float((got.float() - ref.float()).abs().max()))
         dist.barrier()   # the next call may overwrite the output
-    out[rank] = errs
     ps.close()
+    # Head-major output, GQA (16 query heads over 4 K/V heads), causal.
+    ps = PeerShardedAttention(ex, rank, world, (1, 1000, 16, 128), layout="head")
+    q = torch.randn(1, 1000, 16, 128, generator=g, device="cuda").half()
+    k, v = (torch.randn(1, 1000, 4, 128, generator=g, device="cuda").half() for _ in range(2))
+    got = ps(q, k, v, causal=True)
+    ex.synchronize()
+    ref = ex.attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    errs.append(float((got.float() - ref.float()).abs().max()))
+    dist.barrier()
+    ps.close()
+    # head_dim 64 (the LLM adapter's heads), 2 images, fused RMSNorm + RoPE.
+    ps = PeerShardedAttention(ex, rank, world, (2, 512, 16, 64))
+    tab = torch.from_numpy(ax.adapter_rope(512)).cuda()
+    q, k, v = (torch.randn(2, 512, 16, 64, generator=g, device="cuda").half() for _ in range(3))
+    got = ps(q, k, v, qk_norm="rms_rope", rope_table=tab)
+    ex.synchronize()
+    ref = ex.attention(q, k, v, qk_norm="rms_rope", rope_table=tab)
+    torch.cuda.synchronize()
+    errs.append(float((got.float() - ref.float()).abs().max()))
+    dist.barrier()
+    ps.close()
+    out[rank] = errs
     dist.barrier()
     dist.destroy_process_group()
 
@@ -211,13 +233,15 @@ def _peer_worker(rank, world, port, out):
 @needs2
 def test_peer_fused_head_sharded_matches_single_gpu():
     """The attention kernel stores its heads into both ranks' outputs (NVLink);
-    every rank's buffer equals the single-GPU result bit for bit."""
+    every rank's buffer equals the single-GPU result bit for bit: three calls
+    in a row (token-major, norm + RoPE and plain), a head-major GQA causal
+    call with a ragged length, and head_dim 64 over two images."""
     import torch.multiprocessing as mp
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     for rank in (0, 1):
-        assert out[rank] == [0.0, 0.0, 0.0], f"rank {rank}: max differences {out[rank]}"
+        assert out[rank] == [0.0] * 5, f"rank {rank}: max differences {out[rank]}"
 
 
 def _peer_absent_worker(rank, world, port, out):
@@ -260,7 +284,7 @@ def _peer_absent_worker(rank, world, port, out):
 @needs2
 def test_peer_that_never_calls_times_out():
     import torch.multiprocessing as mp
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_peer_absent_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     assert out[0] == "timeout" and out["after"]
