@@ -272,27 +272,42 @@ def run_gpu(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+E2E_INPUTS = (("sq", (1, S_SELF, HEADS, HD)), ("sk", (1, S_SELF, HEADS, HD)), ("sv", (1, S_SELF, HEADS, HD)),
+              ("cq", (1, S_SELF, HEADS, HD)), ("ck", (1, S_CTX, HEADS, HD)), ("cv", (1, S_CTX, HEADS, HD)))
+
+
+def _packed_views(buf):
+    """q/k/v views of one block's packed inputs (E2E_INPUTS order)."""
+    views, off = {}, 0
+    for name, shape in E2E_INPUTS:
+        n = 1
+        for x in shape:
+            n *= x
+        views[name] = buf[off:off + n].view(*shape)
+        off += n
+    return views
+
+
 def run_e2e(torch, ex, device, stream, rope, args, world):
     """Same metric through the fused C-ABI call with pinned host inputs/outputs.
-    Per block: H2D of q,k,v (self) + q,k,v (cross), two fused attention calls,
-    D2H of both outputs; copies and compute overlap across three streams."""
+    Per block: one H2D copy of the block's packed q,k,v (self) + q,k,v (cross),
+    two fused attention calls, one D2H copy of both outputs; copies and compute
+    overlap across three streams."""
     nblk = 4
     g = torch.Generator().manual_seed(99)
-    host = []
-    for _ in range(nblk):
-        host.append({k: torch.randn(*(shape), generator=g).half().pin_memory()
-                     for k, shape in (("sq", (1, S_SELF, HEADS, HD)), ("sk", (1, S_SELF, HEADS, HD)),
-                                      ("sv", (1, S_SELF, HEADS, HD)), ("cq", (1, S_SELF, HEADS, HD)),
-                                      ("ck", (1, S_CTX, HEADS, HD)), ("cv", (1, S_CTX, HEADS, HD)))})
-    outs_h = [torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16).pin_memory() for _ in range(4)]
-    dev_in = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host[0].items()}
-              for _ in range(2)]
-    dev_out = [[torch.empty(1, S_SELF, HEADS, HD, dtype=torch.float16, device=device) for _ in range(2)]
-               for _ in range(2)]
+    n_in = sum(int(torch.Size(shape).numel()) for _, shape in E2E_INPUTS)
+    host = [torch.randn(n_in, generator=g).half().pin_memory() for _ in range(nblk)]
+    n_out = 2 * S_SELF * HEADS * HD
+    outs_h = [torch.empty(n_out, dtype=torch.float16).pin_memory() for _ in range(2)]
+    dev_buf = [torch.empty(n_in, dtype=torch.float16, device=device) for _ in range(2)]
+    dev_in = [_packed_views(b) for b in dev_buf]
+    dev_out_buf = [torch.empty(n_out, dtype=torch.float16, device=device) for _ in range(2)]
+    dev_out = [[b[:n_out // 2].view(1, S_SELF, HEADS, HD), b[n_out // 2:].view(1, S_SELF, HEADS, HD)]
+               for b in dev_out_buf]
     s_in = torch.cuda.Stream(device)
     s_out = torch.cuda.Stream(device)
-    h2d = sum(v.numel() * 2 for v in host[0].values())
-    d2h = 2 * S_SELF * HEADS * HD * 2
+    h2d = n_in * 2
+    d2h = n_out * 2
 
     def one_image():
         in_ready = [None, None]
@@ -305,8 +320,7 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
             with torch.cuda.stream(s_in):
                 if not first[slot]:
                     s_in.wait_event(comp_done[slot])
-                for k, v in src.items():
-                    dev_in[slot][k].copy_(v, non_blocking=True)
+                dev_buf[slot].copy_(src, non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(s_in)
                 in_ready[slot] = ev
@@ -321,8 +335,7 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
             comp_done[slot].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(comp_done[slot])
-                outs_h[2 * slot].copy_(dev_out[slot][0], non_blocking=True)
-                outs_h[2 * slot + 1].copy_(dev_out[slot][1], non_blocking=True)
+                outs_h[slot].copy_(dev_out_buf[slot], non_blocking=True)
                 out_done[slot].record(s_out)
             first[slot] = False
 
