@@ -90,6 +90,8 @@ PROJ_STORE, PROJ_QKV_NORM, PROJ_GATE_ADD = 0, 1, 2
 WEIGHT_FP16, WEIGHT_W8, WEIGHT_W4 = 0, 1, 2
 
 # name -> (restype, argtypes); every symbol the header declares.
+ABI_VERSION = 2  # ANIMAXS_ATTN_ABI_VERSION in include/animaxs_attn.h
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _I64 = ctypes.c_int64
@@ -146,7 +148,7 @@ def lib():
             fn = getattr(handle, name)
             fn.restype = res
             fn.argtypes = args
-        if handle.animaxs_attn_abi_version() != 1:
-            raise ImportError("libanimaxs_attn.so ABI version mismatch")
+        if handle.animaxs_attn_abi_version() != ABI_VERSION:
+            raise ImportError(f"libanimaxs_attn.so ABI version mismatch (want {ABI_VERSION})")
         _lib = handle
     return _lib

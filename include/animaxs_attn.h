@@ -38,7 +38,9 @@
 extern "C" {
 #endif
 
-#define ANIMAXS_ATTN_ABI_VERSION 1
+/* 2: animaxs_proj_desc gained the weight-storage fields (w_storage, w_scale,
+ * w_zero, w_packed_stride); the peer-group and dequant entry points. */
+#define ANIMAXS_ATTN_ABI_VERSION 2
 
 /* Status codes.  The reference throws AnimapkError.validation(String) for every
  * argument problem (AttentionExecutor.swift:778-825) and surfaces GPU errors as

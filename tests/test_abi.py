@@ -22,6 +22,11 @@ def _declared():
     return sorted(set(re.findall(r"\b(animaxs_[a-z0-9_]+)\s*\(", text)))
 
 
+def _header_abi_version():
+    m = re.search(r"#define ANIMAXS_ATTN_ABI_VERSION (\d+)", open(HEADER).read())
+    return int(m.group(1))
+
+
 @pytest.fixture(scope="module")
 def lib():
     from animaxs_b200 import _lib
@@ -39,7 +44,7 @@ def test_library_exports_every_declared_symbol(lib):
     assert not missing, f"declared but not exported: {missing}"
     # and the ctypes binding knows every one of them
     assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
-    assert lib.animaxs_attn_abi_version() == 1
+    assert lib.animaxs_attn_abi_version() == _lib.ABI_VERSION == _header_abi_version()
 
 
 def test_library_links_no_nccl_or_cudart_at_load_time():
