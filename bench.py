@@ -757,7 +757,7 @@ def decode_roofline(pj, bits, device, stream, pool=6, reps=5):
     nbytes = n * k * bits // 8 + 2 * n * (k // 64) * 2 + n * k * 2
     hbm = peaks()[2]
     achieved = nbytes / (per_launch_ms / 1e3) / 1e9
-    return {"kernel": f"dequant_kernel<{bits}> ([6144, 2048] weight, {pool} weights cycled, "
+    return {"kernel": f"dequant_aligned_kernel<{bits}> ([6144, 2048] weight, {pool} weights cycled, "
                       f"{pool * n * k * 2 / 2**20:.0f} MiB of fp16 outputs > L2, {reps * pool} launches "
                       "replayed from a CUDA graph)",
             "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
