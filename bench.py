@@ -726,7 +726,7 @@ def quantize_groups(w, bits):
 
 
 def decode_roofline(pj, bits, device, stream, pool=6, reps=5):
-    """The weight decode alone (dequant_kernel): the DiT q|k|v weight shape
+    """The weight decode alone (dequant_aligned_kernel): the DiT q|k|v weight shape
     [6144, 2048], cycled over `pool` weights whose fp16 outputs total > L2.
     Algorithmic bytes per launch = codes + scale + zero read + fp16 written."""
     import torch
