@@ -12,3 +12,4 @@ from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError, 
 from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  # noqa: F401
                        DitRoPE, GqaHeadMapping, adapter_rope, qwen_rope)
 from .projection import ProjectionExecutor, QuantizedWeight  # noqa: F401,E402
+from .probe import ProbeStats, ScoreProbe  # noqa: F401,E402

@@ -108,6 +108,7 @@ SIGNATURES = {
     "animaxs_attn_scratch_bytes": (_I, [_DESC, ctypes.POINTER(_I64)]),
     "animaxs_attn_query_tiles": (_I, [_P, ctypes.POINTER(_I64)]),
     "animaxs_attn_set_kernel_timing": (_I, [_P, _I]),
+    "animaxs_attn_set_score_probe": (_I, [_P, _P]),
     "animaxs_attn_kernel_timing": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_double),
                                         ctypes.POINTER(ctypes.c_double)]),
     "animaxs_rms_rope_split_half": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I64, ctypes.c_float, _P]),

@@ -20,6 +20,7 @@ struct animaxs_attn_ctx {
   unsigned int* d_status = nullptr;  // device status word written by kernels
   int64_t query_tiles = 0;
   bool timing = false;                        // bracket each attention kernel with events
+  unsigned int* score_probe = nullptr;        // device uint32[4] probe slot, or nullptr
   std::vector<cudaEvent_t> events;            // pool: pairs (start, stop)
   size_t events_used = 0;                     // events recorded since the last read
   std::string last_error;

@@ -318,6 +318,9 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   } restore{ctx->device, prev};
 
   const int64_t D = d->head_dim;
+  if (ctx->score_probe != nullptr && D != 64 && D != 128)
+    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED, "the score probe supports headDim 64 and 128 (got %lld)",
+                        static_cast<long long>(D));
   const void* qa = q;
   const void* ka = k;
   int64_t q_st = d->q_tok_stride, q_sh = d->q_head_stride, q_sb = d->q_batch_stride;
@@ -427,6 +430,7 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     p.o_batch = d->o_batch_stride;
   }
   p.status = ctx->d_status;
+  p.probe = ctx->score_probe;
   if (peers != nullptr) {
     if (peers->n < 0 || peers->n > ax::kMaxPeers || (d->head_dim != 64 && d->head_dim != 128))
       return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "peer stores need head_dim 64 or 128 and <= 7 peers");
@@ -523,6 +527,15 @@ extern "C" int animaxs_attn_selftest_wait_timeout(animaxs_attn_ctx* ctx, int64_t
 extern "C" int animaxs_attn_set_kernel_timing(animaxs_attn_ctx* ctx, int enable) {
   if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
   ctx->timing = enable != 0;
+  return ANIMAXS_OK;
+}
+
+extern "C" int animaxs_attn_set_score_probe(animaxs_attn_ctx* ctx, unsigned int* stats) {
+  if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
+  if (stats != nullptr && reinterpret_cast<uintptr_t>(stats) % 4 != 0)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "probe slot must be 4-byte aligned");
+  ctx->score_probe = stats;
+  ctx->last_error.clear();
   return ANIMAXS_OK;
 }
 

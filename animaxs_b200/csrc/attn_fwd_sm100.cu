@@ -139,7 +139,9 @@ __device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, i
   return (e + kTileN - 1) / kTileN;
 }
 
-template <int HD>
+// kProbe: also record the scores' numerical health (animaxs_attn_set_score_probe);
+// a separate instantiation so that the production kernel carries no trace of it.
+template <int HD, bool kProbe>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -385,6 +387,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("" : AX_RW32(s[3])::"memory");
 
         const int key0 = j * kTileN;
+        if constexpr (kProbe) {
+          // Score health over this row's unmasked keys, as the reference's
+          // attention_softmax_rows_probe (AnimaKernels.metal:1738-1830) records
+          // it for the scaled scores: flags, max |score|, first flagged key.
+          const int lim = p.causal ? min(valid, row + 1) : valid;
+          const float scale = sl2 * 0.6931471805599453f;  // scale_log2 / log2(e)
+          unsigned int pf = 0u, pmax = 0u, pfirst = 0xFFFFFFFFu;
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            const float sv = __uint_as_float(s[c >> 5][c & 31]);
+            if (key0 + c < lim) {
+              unsigned int f = 0u;
+              if (sv != sv) {
+                f = 1u;
+              } else if (isinf(sv)) {
+                f = sv > 0.f ? 2u : 4u;
+              } else {
+                const float a = fabsf(sv) * scale;
+                if (a > 65504.f) f = 8u;
+                pmax = max(pmax, __float_as_uint(a));
+              }
+              if (f != 0u) {
+                pf |= f;
+                pfirst = min(pfirst, static_cast<unsigned int>(key0 + c));
+              }
+            }
+          }
+          pf = __reduce_or_sync(0xffffffffu, pf);
+          pmax = __reduce_max_sync(0xffffffffu, pmax);
+          pfirst = __reduce_min_sync(0xffffffffu, pfirst);
+          if (lane == 0) {
+            if (pf != 0u) {
+              atomicOr(p.probe, pf);
+              atomicMin(p.probe + 2, pfirst);
+            }
+            if (pmax != 0u) atomicMax(p.probe + 1, pmax);
+          }
+        }
         if ((key0 + kTileN > valid) || (p.causal && key0 + kTileN - 1 > row)) {
           const int lim = p.causal ? min(valid, row + 1) : valid;  // keys >= lim are masked
 #pragma unroll
@@ -558,8 +598,11 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   cudaError_t e;
   const uint64_t bit = 1ull << (dev & 63);
   if ((configured.load(std::memory_order_acquire) & bit) == 0) {
-    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Smem<HD>::kBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Smem<HD>::kBytes);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -583,7 +626,10 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
                    p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
     return cudaErrorInvalidValue;
-  attn_fwd_sm100_kernel<HD><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
+  if (q.probe != nullptr)
+    attn_fwd_sm100_kernel<HD, true><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
+  else
+    attn_fwd_sm100_kernel<HD, false><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
   return cudaGetLastError();
 }
 

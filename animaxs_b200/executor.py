@@ -151,6 +151,13 @@ class AttentionExecutor:
         self._check(self._lib.animaxs_attn_query_tiles(self._ctx, ctypes.byref(v)))
         return v.value
 
+    def set_score_probe(self, probe) -> None:
+        """Record the health of every following call's scores into ``probe``
+        (a :class:`~animaxs_b200.probe.ScoreProbe`, or None to stop); the
+        ``monitor``/``probe`` pair of the reference's executor."""
+        ptr = None if probe is None else probe.data_ptr()
+        self._check(self._lib.animaxs_attn_set_score_probe(self._ctx, ptr))
+
     def set_kernel_timing(self, enable: bool):
         """Bracket every flash-kernel launch with CUDA events (see kernel_timing)."""
         self._check(self._lib.animaxs_attn_set_kernel_timing(self._ctx, 1 if enable else 0))
@@ -224,8 +231,10 @@ class AttentionExecutor:
     def encode(self, stream, query, key, value, output, *, heads: int, query_count: int,
                key_count: int, head_dim: int, query_offset: int = 0, key_offset: int = 0,
                value_offset: int = 0, output_offset: int = 0, key_value_heads: int | None = None,
-               causal: bool = False, layout: AttentionInputLayout | None = None, **ext):
-        """AttentionExecutor.encode (AttentionExecutor.swift:122-302): enqueue on ``stream``."""
+               causal: bool = False, layout: AttentionInputLayout | None = None, probe=None, **ext):
+        """AttentionExecutor.encode (AttentionExecutor.swift:122-302): enqueue on ``stream``.
+        ``probe`` (a :class:`~animaxs_b200.probe.ScoreProbe`) records this
+        call's score health, as the reference's ``probe:`` argument."""
         offsets = (query_offset, key_offset, value_offset, output_offset)
         if min(offsets) < 0:
             raise AttentionValidationError(_lib.ERR_INVALID_ARG,
@@ -238,8 +247,14 @@ class AttentionExecutor:
         d = self.make_desc(heads=heads, query_count=query_count, key_count=key_count,
                            head_dim=head_dim, key_value_heads=key_value_heads, causal=causal,
                            layout=layout, lengths=tuple(lens), **ext)
-        rc = self._lib.animaxs_attn_forward(self._ctx, ctypes.byref(d), *[ctypes.c_void_p(p) for p in ptrs],
-                                            _stream_handle(stream))
+        if probe is not None:
+            self.set_score_probe(probe)
+        try:
+            rc = self._lib.animaxs_attn_forward(self._ctx, ctypes.byref(d), *[ctypes.c_void_p(p) for p in ptrs],
+                                                _stream_handle(stream))
+        finally:
+            if probe is not None:
+                self._lib.animaxs_attn_set_score_probe(self._ctx, None)
         self._check(rc)
 
     def strided_desc(self, q, k, v, out, *, causal=False, qk_norm="none", rope_table=None,

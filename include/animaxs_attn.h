@@ -186,6 +186,29 @@ int animaxs_attn_set_kernel_timing(animaxs_attn_ctx* ctx, int enable);
 int animaxs_attn_kernel_timing(animaxs_attn_ctx* ctx, int64_t* launches, double* total_ms,
                                double* max_ms);
 
+/* Numerical health of the attention scores: the reference's score probes
+ * (NumericalMonitor .selfScores / .crossScores, bound by encode(probe:) to
+ * attention_softmax_rows_probe, AttentionExecutor.swift:148,266 and
+ * AnimaKernels.metal:1738-1830).  While `stats` is set, every forward call on
+ * this context folds the health of its scaled scores (scale * q.k over the
+ * unmasked keys) into the probe slot `stats`, DEVICE uint32[4] with the
+ * reference's layout (NumericalMonitor.swift:17-119):
+ *   [0] |= flags    ANIMAXS_PROBE_* below
+ *   [1]  = max of the float bits of |score| over the finite scores
+ *   [2]  = min key index of a flagged score (initialise to 0xFFFFFFFF)
+ *   [3]    unused
+ * The words are updated with device atomics in stream order; NULL turns the
+ * probe off.  Head dims 64 and 128 (the DiT and adapter calls); set with head
+ * dim 256 or 384 a forward call returns ANIMAXS_ERR_UNSUPPORTED.  The
+ * reference's scores are fp16 (a score beyond 65504 is stored as Inf there);
+ * here they are fp32, so such a score raises ANIMAXS_PROBE_HALF_OVERFLOW and
+ * keeps its magnitude. */
+#define ANIMAXS_PROBE_NAN 1u
+#define ANIMAXS_PROBE_POS_INF 2u
+#define ANIMAXS_PROBE_NEG_INF 4u
+#define ANIMAXS_PROBE_HALF_OVERFLOW 8u
+int animaxs_attn_set_score_probe(animaxs_attn_ctx* ctx, unsigned int* stats);
+
 /* Standalone per-(token, head) RMSNorm + split-half RoPE, fp16 in/out
  * ([tokens, heads, head_dim] rows, `row_stride` elements apart per token),
  * in place allowed.  Replaces kernel rms_rope_split_half

@@ -28,6 +28,9 @@ AnimaXS project):
                             path of ``attention_pytorch``)
 * masks ................... ``scripts/qwen_comfy_oracle.py:238-248``: additive
                             ``finfo.min / 4`` for causal (``triu(1)``) and key padding
+* score-health probe ...... ``AnimaXS/Shaders/AnimaKernels.metal:1738-1830``
+                            (``attention_softmax_rows_probe``; slot layout
+                            ``AnimaXS/Runtime/Diagnostics/NumericalMonitor.swift:136-161``)
 * W4/W8 weight decode ..... ``scripts/animapk_cuda/quant.py:32-76``
                             (``decode_w4_matrix`` / ``decode_w8_matrix``),
                             ``AnimaXS/Shaders/AnimaKernels.metal:19-67``
@@ -349,3 +352,53 @@ def dequant_to_half(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray, *, 
     ze = np.asarray(zero, dtype=np.float16).astype(np.float32)[:, g]
     prod = (q.astype(np.float32) * sc).astype(np.float32)
     return (prod + ze).astype(np.float32).astype(np.float16)
+
+
+# ---------------------------------------------------------------------------
+# Score-health probe
+# ---------------------------------------------------------------------------
+PROBE_NAN, PROBE_POS_INF, PROBE_NEG_INF, PROBE_HALF_OVERFLOW = 1, 2, 4, 8
+
+
+def score_health(q: np.ndarray, k: np.ndarray, *, scale: float | None = None, causal: bool = False,
+                 kv_valid_len=None) -> tuple[int, float, int]:
+    """(flags, max |score|, first flagged key) of the scaled scores
+    ``scale * q.k`` over each row's unmasked keys, as the reference's
+    attention_softmax_rows_probe records them (AnimaKernels.metal:1738-1830):
+    NaN, +Inf, -Inf, and |score| > 65504 flag a score; the magnitude is the
+    largest |score| among the finite ones; the index is the smallest flagged
+    key column (0xFFFFFFFF when none).  Scores here are fp32 (the reference
+    rounds them to fp16 first).  ``q``/``k`` are ``[B, S, H, D]`` (GQA by
+    ``gqa_kv_head``)."""
+    qf = np.asarray(q, dtype=np.float32)
+    kf = np.asarray(k, dtype=np.float32)
+    b, sq, hq, d = qf.shape
+    sk, hkv = kf.shape[1], kf.shape[2]
+    scale = 1.0 / np.sqrt(d) if scale is None else scale
+    flags, max_abs, first = 0, 0.0, 0xFFFFFFFF
+    with np.errstate(invalid="ignore", over="ignore"):
+        for bi in range(b):
+            valid = sk if kv_valid_len is None else int(kv_valid_len[bi] if np.ndim(kv_valid_len) else kv_valid_len)
+            for h in range(hq):
+                kh = gqa_kv_head(h, hq, hkv)
+                s = (qf[bi, :, h, :] @ kf[bi, :, kh, :].T).astype(np.float32)   # [sq, sk] raw q.k
+                mask = np.broadcast_to(np.arange(sk)[None, :] < valid, s.shape)
+                if causal:
+                    mask = mask & (np.arange(sk)[None, :] <= np.arange(sq)[:, None])
+                sv = s[mask]
+                cols = np.broadcast_to(np.arange(sk)[None, :], s.shape)[mask]
+                nan = np.isnan(sv)
+                pinf = np.isposinf(sv)
+                ninf = np.isneginf(sv)
+                finite = np.isfinite(sv)
+                a = np.abs(sv[finite]) * np.float32(scale)
+                over = np.zeros_like(sv, dtype=bool)
+                over[finite] = a > 65504.0
+                flags |= (PROBE_NAN if nan.any() else 0) | (PROBE_POS_INF if pinf.any() else 0) | \
+                    (PROBE_NEG_INF if ninf.any() else 0) | (PROBE_HALF_OVERFLOW if over.any() else 0)
+                if a.size:
+                    max_abs = max(max_abs, float(a.max()))
+                bad = nan | pinf | ninf | over
+                if bad.any():
+                    first = min(first, int(cols[bad].min()))
+    return flags, max_abs, first

@@ -254,6 +254,29 @@ def test_peer_group_rejects_bad_arguments(lib):
     assert lib.animaxs_attn_forward_head_sharded_peer(None, None, None, 0, 0, 0, 0, None) == -1
 
 
+def test_score_probe_requires_context(lib):
+    assert lib.animaxs_attn_set_score_probe(None, None) == -1
+
+
+def test_probe_stats_decoding_follows_the_reference():
+    """NumericalMonitor.Stats (NumericalMonitor.swift:136-161): flag bits,
+    max |score| from its float bits, condition wording and precedence."""
+    from animaxs_b200.probe import ProbeStats
+    assert ProbeStats.from_words([0, 0, 0xFFFFFFFF, 0]) == ProbeStats()
+    assert not ProbeStats().has_issue
+    st = ProbeStats.from_words([8 | 2, 0x47CA0000, 42, 0])
+    assert st.has_half_overflow and st.has_pos_inf and st.first_index == 42
+    assert st.max_abs == 103424.0
+    assert st.condition == "positive Inf detected"
+    assert ProbeStats(flags=1 | 4).condition == "NaN detected"
+    assert ProbeStats(flags=4).condition == "negative Inf detected"
+    assert ProbeStats(flags=8).condition == "value exceeded FP16 finite range"
+    import re
+    h = open(HEADER).read()
+    got = {n: int(v) for n, v in re.findall(r"#define ANIMAXS_PROBE_(\w+) (\d+)u", h)}
+    assert got == {"NAN": 1, "POS_INF": 2, "NEG_INF": 4, "HALF_OVERFLOW": 8}
+
+
 def test_selftest_rejects_bad_timeout(lib):
     """The failure-detection self-test validates its limit before touching a device."""
     assert lib.animaxs_attn_selftest_wait_timeout(None, 1000, None) == -1

@@ -206,3 +206,22 @@ def test_quant_decode_oracle_layout():
     w8 = ora.dequant_to_half(np.array([[255, 7]], dtype=np.uint8), np.array([[0.25]], dtype=np.float16),
                              np.array([[-1.0]], dtype=np.float16), bits=8, k=2)
     assert w8[0, 0] == np.float16(62.75) and w8[0, 1] == np.float16(0.75)
+
+
+def test_score_health_oracle():
+    """score_health on planted values: flags, magnitude over finite scores,
+    first flagged key, masks (key padding and causal) excluded."""
+    rng = np.random.default_rng(0)
+    q = (np.abs(rng.standard_normal((1, 8, 2, 64))) + 0.1).astype(np.float16)
+    k = rng.standard_normal((1, 8, 2, 64)).astype(np.float16)
+    flags, mx, first = ora.score_health(q, k)
+    assert flags == 0 and first == 0xFFFFFFFF and mx > 0
+    k2 = k.copy()
+    k2[0, 5, 1, :] = np.inf
+    k2[0, 6, 0, :] = -np.inf
+    assert ora.score_health(q, k2) == (ora.PROBE_POS_INF | ora.PROBE_NEG_INF, mx, 5)
+    k3 = k.copy()
+    k3[0, 3, 0, 0] = np.nan
+    assert ora.score_health(q, k3)[0::2] == (ora.PROBE_NAN, 3)
+    assert ora.score_health(q, k3, kv_valid_len=3)[0::2] == (0, 0xFFFFFFFF)
+    assert ora.score_health(q, k3, causal=True)[0::2] == (ora.PROBE_NAN, 3)
