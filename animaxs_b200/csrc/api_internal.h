@@ -9,6 +9,16 @@
 #include <vector>
 
 #include "../../include/animaxs_attn.h"
+#include <nvtx3/nvToolsExt.h>
+
+// NVTX range around a C ABI call (header-only NVTX v3: a no-op unless a
+// profiler injects itself), so a capture can attribute kernels to the call.
+struct AxRange {
+  explicit AxRange(const char* name) { nvtxRangePushA(name); }
+  ~AxRange() { nvtxRangePop(); }
+  AxRange(const AxRange&) = delete;
+  AxRange& operator=(const AxRange&) = delete;
+};
 
 struct animaxs_attn_ctx {
   int device = 0;

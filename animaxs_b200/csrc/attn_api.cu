@@ -466,6 +466,7 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
 extern "C" int animaxs_attn_forward(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d,
                                     const void* q, const void* k, const void* v, void* o,
                                     void* stream) {
+  AxRange range("animaxs_attn_forward");
   if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
   int rc = ax_validate(ctx, d, q, k, v, o);
   if (rc != ANIMAXS_OK) return rc;

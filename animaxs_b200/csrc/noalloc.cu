@@ -67,6 +67,7 @@ int scratch_address(int dev, void** out) {
 extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const void* q,
                                             const void* k, const void* v, void* o,
                                             void* stream_) {
+  AxRange range("animaxs_attn_forward_noalloc");
   int rc = ax_validate(nullptr, d, q, k, v, o);
   if (rc != ANIMAXS_OK) return rc;
   int64_t need = 0;

@@ -183,6 +183,7 @@ extern "C" int animaxs_peer_group_destroy(animaxs_peer_group* g) {
 extern "C" int animaxs_attn_forward_head_sharded_peer(animaxs_attn_ctx* ctx, animaxs_peer_group* g,
                                                       const animaxs_attn_desc* d, const void* q, const void* k,
                                                       const void* v, void* o, void* stream_) {
+  AxRange range("animaxs_attn_forward_head_sharded_peer");
   if (ctx == nullptr || g == nullptr) return ANIMAXS_ERR_INVALID_ARG;
   int rc = ax_validate(ctx, d, q, k, v, o);
   if (rc != ANIMAXS_OK) return rc;

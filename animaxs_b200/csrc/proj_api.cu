@@ -154,6 +154,7 @@ extern "C" int animaxs_proj_validate(animaxs_attn_ctx* ctx, const animaxs_proj_d
 extern "C" int animaxs_dequant_to_half(animaxs_attn_ctx* ctx, int bits, const void* packed, const void* scale,
                                        const void* zero, void* out, int rows, int k, int64_t packed_stride,
                                        int64_t out_stride, void* stream) {
+  AxRange range("animaxs_dequant_to_half");
   if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
   int rc = dequant_validate(ctx, bits, packed, scale, zero, out, rows, k, packed_stride, out_stride);
   if (rc != ANIMAXS_OK) return rc;
@@ -170,6 +171,7 @@ extern "C" int animaxs_dequant_to_half(animaxs_attn_ctx* ctx, int bits, const vo
 
 extern "C" int animaxs_proj_forward(animaxs_attn_ctx* ctx, const animaxs_proj_desc* d, const void* x,
                                     const void* w, void* out, void* stream) {
+  AxRange range("animaxs_proj_forward");
   if (ctx == nullptr) return ANIMAXS_ERR_INVALID_ARG;
   int rc = proj_validate(ctx, d, x, w, out);
   if (rc != ANIMAXS_OK) return rc;

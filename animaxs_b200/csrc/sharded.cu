@@ -176,6 +176,7 @@ extern "C" int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_
                                                  const animaxs_attn_desc* d, const void* q,
                                                  const void* k, const void* v, void* o,
                                                  void* stream_) {
+  AxRange range("animaxs_attn_forward_head_sharded");
   if (ctx == nullptr || comm == nullptr) return ANIMAXS_ERR_INVALID_ARG;
   int rc = ax_validate(ctx, d, q, k, v, o);
   if (rc != ANIMAXS_OK) return rc;
