@@ -141,12 +141,7 @@ __device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, i
 
 // kProbe: also record the scores' numerical health (animaxs_attn_set_score_probe);
 // a separate instantiation so that the production kernel carries no trace of it.
-// kHalfP: P is published in two halves, and PV issued in two halves, so that
-// the first half of PV runs while the softmax computes the second (long key
-// ranges).  With at most four key tiles per item (cross-attention to a
-// 512-token context) one publication and one wait per tile is faster: the
-// MMA warp's wait costs more there than the overlap gains (measured ~5 %).
-template <int HD, bool kProbe, bool kHalfP>
+template <int HD, bool kProbe>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -313,10 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 0), pph, abort_flag, p.status))) break;
           tc_fence_after();
           issue_pv_half<HD>(tmem + kColO, tmem + 0, vt, 0, j > 0);
-          if (kHalfP) {
-            if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 1), pph, abort_flag, p.status))) break;
-            tc_fence_after();
-          }
+          if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 1), pph, abort_flag, p.status))) break;
+          tc_fence_after();
           issue_pv_half<HD>(tmem + kColO, tmem + 0, vt, 1, true);
           if (j == nA - 1) tc_commit_warp(BAR(kBarODone + 0));
         }
@@ -333,10 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 2), pph, abort_flag, p.status))) break;
           tc_fence_after();
           issue_pv_half<HD>(tmem + kColO + HD, tmem + 128, vt, 0, j > 0);
-          if (kHalfP) {
-            if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 3), pph, abort_flag, p.status))) break;
-            tc_fence_after();
-          }
+          if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 3), pph, abort_flag, p.status))) break;
+          tc_fence_after();
           issue_pv_half<HD>(tmem + kColO + HD, tmem + 128, vt, 1, true);
           if (j == nB - 1) tc_commit_warp(BAR(kBarODone + 1));
         }
@@ -496,14 +487,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
             pk[half][(c >> 1) & 31] = pack_half2(pr.x, pr.y);
           }
+          // Publish this half of P: the MMA warp starts its half of PV_X(j) while
+          // the second half is still being computed.
           tmem_st32(s_addr + half * 32, pk[half]);
-          if (kHalfP || half == 1) {
-            // Publish P (this half, or both): the MMA warp starts PV_X(j) (its
-            // first half while the second half of P is still being computed).
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(BAR(kBarPHalf + 2 * X + (kHalfP ? half : 0)));
-          }
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(BAR(kBarPHalf + 2 * X + half));
         }
         const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
         const float2 a = add2(a01, a23);
@@ -609,11 +598,12 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   cudaError_t e;
   const uint64_t bit = 1ull << (dev & 63);
   if ((configured.load(std::memory_order_acquire) & bit) == 0) {
-    for (auto* fn : {attn_fwd_sm100_kernel<HD, false, true>, attn_fwd_sm100_kernel<HD, false, false>,
-                     attn_fwd_sm100_kernel<HD, true, true>, attn_fwd_sm100_kernel<HD, true, false>}) {
-      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<HD>::kBytes);
-      if (e != cudaSuccess) return e;
-    }
+    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Smem<HD>::kBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Smem<HD>::kBytes);
+    if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   // Persistent grid: one CTA per SM (at most one per work item).
@@ -636,11 +626,10 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
                    p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
     return cudaErrorInvalidValue;
-  // One P publication per tile when no item has more than four key tiles.
-  const bool half_p = p.kv_len > 4 * kTileN;
-  auto* kern = q.probe != nullptr ? (half_p ? attn_fwd_sm100_kernel<HD, true, true> : attn_fwd_sm100_kernel<HD, true, false>)
-                                  : (half_p ? attn_fwd_sm100_kernel<HD, false, true> : attn_fwd_sm100_kernel<HD, false, false>);
-  kern<<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
+  if (q.probe != nullptr)
+    attn_fwd_sm100_kernel<HD, true><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
+  else
+    attn_fwd_sm100_kernel<HD, false><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
   return cudaGetLastError();
 }
 
