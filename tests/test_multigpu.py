@@ -290,6 +290,24 @@ def test_peer_that_never_calls_times_out():
     assert out[0] == "timeout" and out["after"]
 
 
+def test_peer_sharded_rejects_bad_shape_before_touching_a_device():
+    """PeerShardedAttention checks its output shape and layout before any
+    library or device call."""
+    from animaxs_b200 import AttentionValidationError
+    from animaxs_b200.sharded import PeerShardedAttention
+
+    class NoDevice:
+        handle = None
+        device = 0
+
+        def last_error(self):
+            return ""
+    with pytest.raises(AttentionValidationError):
+        PeerShardedAttention(NoDevice(), 0, 2, (1, 2, 3))
+    with pytest.raises(AttentionValidationError):
+        PeerShardedAttention(NoDevice(), 0, 2, (1, 8, 2, 64), layout="diagonal")
+
+
 def test_config4_prompt_seeds_are_disjoint_across_ranks():
     """Batch sharding: every (prompt, step, block) has its own seed."""
     from oracle.inputs import workload_seed
