@@ -259,7 +259,10 @@ def run_gpu(args, rank, world, local_rank):
                      "flops_per_launch": BATCH * SELF_FLOPS, "avg_launch_ms": avg_kern,
                      "max_launch_ms": kern_max_ms, "launches_timed": n_kern,
                      "traffic": TRAFFIC_PER_LAUNCH_MB * 1e6, "traffic_unit": "bytes per launch",
-                     "algorithmic_bytes": BATCH * 4 * S_SELF * HEADS * HD * 2},
+                     "algorithmic_bytes": BATCH * 4 * S_SELF * HEADS * HD * 2,
+                     # secondary figure: the ncu DRAM bytes per launch over the timed launch
+                     "hbm_gbs": TRAFFIC_PER_LAUNCH_MB * 1e6 / (avg_kern / 1e3) / 1e9,
+                     "hbm_frac": TRAFFIC_PER_LAUNCH_MB * 1e6 / (avg_kern / 1e3) / 1e9 / peaks()[2]},
         "clocks": clocks,
         "gpu_launches": launches,
         "e2e": e2e,
