@@ -254,6 +254,28 @@ def test_peer_group_rejects_bad_arguments(lib):
     assert lib.animaxs_attn_forward_head_sharded_peer(None, None, None, 0, 0, 0, 0, None) == -1
 
 
+def test_header_compiles_as_c11_and_cxx17(tmp_path):
+    """The header is consumed by C (and a Swift module map): it must compile as
+    strict C11 as well as C++17, with every declaration usable."""
+    src = tmp_path / "use.c"
+    src.write_text(
+        '#include "animaxs_attn.h"\n'
+        "int main(void) {\n"
+        "  animaxs_attn_desc d; animaxs_proj_desc p; unsigned int stats[4];\n"
+        "  (void)animaxs_attn_desc_init(&d, 1, 16, 16, 4096, 4096, 128);\n"
+        "  (void)animaxs_proj_desc_init(&p, 256, 768, 256, ANIMAXS_PROJ_QKV_NORM);\n"
+        "  p.w_storage = ANIMAXS_WEIGHT_W4;\n"
+        "  (void)animaxs_attn_set_score_probe((animaxs_attn_ctx*)0, stats);\n"
+        "  animaxs_peer_group* g = (animaxs_peer_group*)0; (void)animaxs_peer_group_output(g);\n"
+        "  return ANIMAXS_ATTN_ABI_VERSION == 2 && ANIMAXS_PROBE_NAN == 1u ? 0 : 1;\n"
+        "}\n")
+    inc = os.path.dirname(HEADER)
+    for cmd in (["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic", "-fsyntax-only"],
+                ["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x", "c++"]):
+        res = subprocess.run([*cmd, "-I", inc, str(src)], capture_output=True, text=True)
+        assert res.returncode == 0, res.stderr
+
+
 def test_score_probe_requires_context(lib):
     assert lib.animaxs_attn_set_score_probe(None, None) == -1
 
