@@ -157,6 +157,7 @@ class AttentionExecutor:
         ``monitor``/``probe`` pair of the reference's executor."""
         ptr = None if probe is None else probe.data_ptr()
         self._check(self._lib.animaxs_attn_set_score_probe(self._ctx, ptr))
+        self._score_probe = probe
 
     def set_kernel_timing(self, enable: bool):
         """Bracket every flash-kernel launch with CUDA events (see kernel_timing)."""
@@ -247,14 +248,15 @@ class AttentionExecutor:
         d = self.make_desc(heads=heads, query_count=query_count, key_count=key_count,
                            head_dim=head_dim, key_value_heads=key_value_heads, causal=causal,
                            layout=layout, lengths=tuple(lens), **ext)
+        outer = getattr(self, "_score_probe", None)
         if probe is not None:
-            self.set_score_probe(probe)
+            self._check(self._lib.animaxs_attn_set_score_probe(self._ctx, probe.data_ptr()))
         try:
             rc = self._lib.animaxs_attn_forward(self._ctx, ctypes.byref(d), *[ctypes.c_void_p(p) for p in ptrs],
                                                 _stream_handle(stream))
         finally:
-            if probe is not None:
-                self._lib.animaxs_attn_set_score_probe(self._ctx, None)
+            if probe is not None:  # back to the probe set with set_score_probe, if any
+                self._lib.animaxs_attn_set_score_probe(self._ctx, None if outer is None else outer.data_ptr())
         self._check(rc)
 
     def strided_desc(self, q, k, v, out, *, causal=False, qk_norm="none", rope_table=None,
