@@ -4,7 +4,8 @@ The product is ``libanimaxs_attn.so`` (C ABI, ``include/animaxs_attn.h``); this
 package holds its CUDA sources (``csrc/``), the in-tree build
 (``build.py``) and the host-side mirror of the reference's Swift
 ``AttentionExecutor`` interface (``executor.py``), plus the fused attention
-projections (``projection.py``).
+projections (``projection.py``) and the cross-attention K/V cache
+(``cross_kv_cache.py``).
 """
 
 from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError,  # noqa: F401
@@ -13,3 +14,4 @@ from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  #
                        DitRoPE, GqaHeadMapping, adapter_rope, qwen_rope)
 from .projection import ProjectionExecutor, QuantizedWeight  # noqa: F401,E402
 from .probe import ProbeStats, ScoreProbe  # noqa: F401,E402
+from .cross_kv_cache import CrossKVCache  # noqa: F401,E402

@@ -23,6 +23,7 @@ ERR_OVERFLOW = -8
 ERR_SCRATCH_LIMIT = -9
 
 QK_NONE, QK_RMS, QK_RMS_ROPE = 0, 1, 2
+NUMERICS_LEGACY, NUMERICS_FP32, NUMERICS_BF16 = 0, 1, 2
 
 
 class AttentionError(RuntimeError):
@@ -69,7 +70,7 @@ class AttnDesc(ctypes.Structure):
         ("q_norm_weight", ctypes.c_void_p), ("k_norm_weight", ctypes.c_void_p),
         ("rope_table", ctypes.c_void_p), ("rope_rows", ctypes.c_int32), ("qk_norm_targets", ctypes.c_int32),
         ("q_bytes", ctypes.c_int64), ("k_bytes", ctypes.c_int64), ("v_bytes", ctypes.c_int64),
-        ("o_bytes", ctypes.c_int64),
+        ("o_bytes", ctypes.c_int64), ("numerics", ctypes.c_int32),
     ]
 
 
@@ -90,7 +91,7 @@ PROJ_STORE, PROJ_QKV_NORM, PROJ_GATE_ADD = 0, 1, 2
 WEIGHT_FP16, WEIGHT_W8, WEIGHT_W4 = 0, 1, 2
 
 # name -> (restype, argtypes); every symbol the header declares.
-ABI_VERSION = 2  # ANIMAXS_ATTN_ABI_VERSION in include/animaxs_attn.h
+ABI_VERSION = 3  # ANIMAXS_ATTN_ABI_VERSION in include/animaxs_attn.h
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -126,7 +127,17 @@ SIGNATURES = {
     "animaxs_peer_group_destroy": (_I, [_P]),
     "animaxs_attn_forward_head_sharded_peer": (_I, [_P, _P, _DESC, _P, _P, _P, _P, _P]),
     "animaxs_attn_forward_noalloc": (_I, [_DESC, _P, _P, _P, _P, _P]),
+    "animaxs_attn_noalloc_status": (_I, []),
     "animaxs_attn_selftest_wait_timeout": (_I, [_P, _I64, _P]),
+    "animaxs_cross_kv_cache_bytes": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I64)]),
+    "animaxs_cross_kv_cache_create": (_I, [_P, _I, _I, _I, _I, _I, _P, _I64, ctypes.POINTER(_P)]),
+    "animaxs_cross_kv_cache_destroy": (_I, [_P]),
+    "animaxs_cross_kv_cache_fill": (_I, [_P, _I, _P, _I64, _I64, _P, _I64, _I64, _I, _P, ctypes.c_float, _P]),
+    "animaxs_cross_kv_cache_project": (_I, [_P, _I, _P, _I64, _I, _P, _I64, _P, ctypes.c_float, _P]),
+    "animaxs_cross_kv_cache_block": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_I64),
+                                          ctypes.POINTER(_I64), ctypes.POINTER(_I)]),
+    "animaxs_cross_kv_cache_mark_ready": (_I, [_P, _I, _I]),
+    "animaxs_cross_kv_cache_reset": (_I, [_P]),
     "animaxs_proj_desc_init": (_I, [ctypes.POINTER(ProjDesc), _I, _I, _I, _I]),
     "animaxs_proj_validate": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P]),
     "animaxs_proj_forward": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P, _P]),

@@ -17,9 +17,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libanimaxs_attn.so")
+CALL_BENCH = os.path.join(BUILD, "call_bench")
 SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "attn_wide_sm100.cu", "qk_norm.cu", "sharded.cu",
            "noalloc.cu", "proj_api.cu", "proj_sm100.cu", "dequant_sm100.cu",
-           "peer_sync.cu", "peer_sharded.cu"]
+           "peer_sync.cu", "peer_sharded.cu", "cross_kv_cache.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
          "--expt-relaxed-constexpr", "-Xptxas", "-v"]
@@ -110,6 +111,17 @@ def build(force: bool = False, verbose: bool = False) -> str:
             sys.stderr.write(res.stdout + res.stderr)
             raise RuntimeError("link failed")
         os.replace(LIB + ".tmp", LIB)
+    # The C-ABI call-cost harness bench.py runs (csrc/call_bench.cu), linked
+    # against the library beside this file.
+    src = os.path.join(CSRC, "call_bench.cu")
+    if force or not _newer(CALL_BENCH, [src, LIB] + headers):
+        cmd = [cc, *ARCH, "-O2", "-std=c++17", "-o", CALL_BENCH + ".tmp", src, "-L" + HERE, "-lanimaxs_attn",
+               "-Xlinker", "-rpath=$ORIGIN/.."]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            sys.stderr.write(res.stdout + res.stderr)
+            raise RuntimeError("call_bench build failed")
+        os.replace(CALL_BENCH + ".tmp", CALL_BENCH)
     return LIB
 
 

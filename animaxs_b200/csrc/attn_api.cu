@@ -185,6 +185,14 @@ int ax_validate(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q
   if (d->qk_norm_targets < ANIMAXS_QK_NORM_BOTH || d->qk_norm_targets > ANIMAXS_QK_NORM_K_ONLY)
     return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown qk_norm_targets %d",
                         d->qk_norm_targets);
+  if (d->numerics < ANIMAXS_NUMERICS_LEGACY || d->numerics > ANIMAXS_NUMERICS_BF16_COMPUTE)
+    return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "unknown numerics %d", d->numerics);
+  if (d->numerics == ANIMAXS_NUMERICS_BF16_COMPUTE)
+    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
+                        "bf16Compute numerics emulates Apple5 BF16 rounding and is not built for B200");
+  if (wide && d->numerics == ANIMAXS_NUMERICS_FP32_SCORES_AND_SOFTMAX)
+    return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
+                        "fp32ScoresAndSoftmax numerics requires headDim 64 or 128 (got %d)", d->head_dim);
   if (wide && d->qk_norm != ANIMAXS_QK_NONE)
     return ax_set_error(ctx, ANIMAXS_ERR_UNSUPPORTED,
                         "fused q/k normalisation requires headDim 128 or 64 (got %d)", d->head_dim);
@@ -291,12 +299,15 @@ int ax_make_tmap(animaxs_attn_ctx* ctx, CUtensorMap* map, const void* base, int6
 // ------------------------------------------------------------------ forward --
 extern "C" int animaxs_attn_scratch_bytes(const animaxs_attn_desc* d, int64_t* bytes) {
   if (d == nullptr || bytes == nullptr) return ANIMAXS_ERR_INVALID_ARG;
-  if (d->qk_norm == ANIMAXS_QK_NONE) {
-    *bytes = 0;
-    return ANIMAXS_OK;
-  }
-  const int64_t q = static_cast<int64_t>(d->batch) * d->q_len * d->heads * d->head_dim * 2;
-  const int64_t k = static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads * d->head_dim * 2;
+  *bytes = 0;
+  if (d->qk_norm == ANIMAXS_QK_NONE) return ANIMAXS_OK;
+  // Only the copies the prologue writes: q unless the caller normalised it,
+  // k unless the caller normalised it (qk_norm_targets); k follows q at a
+  // 256-byte boundary.
+  const bool norm_q = d->qk_norm_targets != ANIMAXS_QK_NORM_K_ONLY;
+  const bool norm_k = d->qk_norm_targets != ANIMAXS_QK_NORM_Q_ONLY;
+  const int64_t q = norm_q ? static_cast<int64_t>(d->batch) * d->q_len * d->heads * d->head_dim * 2 : 0;
+  const int64_t k = norm_k ? static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads * d->head_dim * 2 : 0;
   *bytes = ((q + 255) & ~static_cast<int64_t>(255)) + k;
   return ANIMAXS_OK;
 }
@@ -325,16 +336,21 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   const void* ka = k;
   int64_t q_st = d->q_tok_stride, q_sh = d->q_head_stride, q_sb = d->q_batch_stride;
   int64_t k_st = d->k_tok_stride, k_sh = d->k_head_stride, k_sb = d->k_batch_stride;
+  const int rows_per_cta = ax::attn_fwd_rows_per_cta();
+  const int n_q_tiles = (d->q_len + rows_per_cta - 1) / rows_per_cta;
 
   if (d->qk_norm != ANIMAXS_QK_NONE) {
-    int64_t need = 0;
-    animaxs_attn_scratch_bytes(d, &need);
-    int rc = ax_ensure_scratch(ctx, static_cast<size_t>(need));
-    if (rc != ANIMAXS_OK) return rc;
+    const bool norm_q = d->qk_norm_targets != ANIMAXS_QK_NORM_K_ONLY;
+    const bool norm_k = d->qk_norm_targets != ANIMAXS_QK_NORM_Q_ONLY;
     const int64_t q_bytes = static_cast<int64_t>(d->batch) * d->q_len * d->heads * D * 2;
+    const int64_t k_bytes = static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads * D * 2;
+    // Layout as animaxs_attn_scratch_bytes counts it: q's copy, then k's at
+    // the next 256-byte boundary (each only when the prologue writes it).
+    const int64_t k_off = ((norm_q ? q_bytes : 0) + 255) & ~static_cast<int64_t>(255);
+    int rc = ax_ensure_scratch(ctx, static_cast<size_t>(k_off + (norm_k ? k_bytes : 0)));
+    if (rc != ANIMAXS_OK) return rc;
     __half* qn = static_cast<__half*>(ctx->scratch);
-    __half* kn = reinterpret_cast<__half*>(static_cast<char*>(ctx->scratch) +
-                                           ((q_bytes + 255) & ~static_cast<int64_t>(255)));
+    __half* kn = reinterpret_cast<__half*>(static_cast<char*>(ctx->scratch) + k_off);
     NormParams np{};
     np.head_dim = static_cast<int>(d->head_dim);
     np.eps = d->eps > 0.f ? d->eps : 1e-6f;
@@ -372,15 +388,15 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
     jk.weight = static_cast<const __half*>(d->k_norm_weight);
     jk.rows = static_cast<int64_t>(d->batch) * d->kv_len * kv_count;
     // The caller may hold an already normalised q or k (qk_norm_targets).
-    const bool norm_q = d->qk_norm_targets != ANIMAXS_QK_NORM_K_ONLY;
-    const bool norm_k = d->qk_norm_targets != ANIMAXS_QK_NORM_Q_ONLY;
     const NormJob q_job = jq, k_job = jk;
     np.njobs = 0;
     if (norm_q) np.job[np.njobs++] = q_job;
     if (norm_k) np.job[np.njobs++] = k_job;
     np.status = ctx->d_status;
-    cudaError_t e = ax::launch_qk_norm(np, stream);
-    if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "qk_norm launch");
+    if (np.njobs > 0) {
+      cudaError_t e = ax::launch_qk_norm(np, stream);
+      if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "qk_norm launch");
+    }
     if (norm_q) {
       qa = qn;
       q_st = q_job.out_tok;
@@ -412,8 +428,7 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   p.kv_valid = d->kv_valid_len > 0 ? d->kv_valid_len : d->kv_len;
   p.kv_valid_dev = d->kv_valid_lens;
   p.causal = d->causal ? 1 : 0;
-  const int rows_per_cta = ax::attn_fwd_rows_per_cta();
-  p.n_q_tiles = (d->q_len + rows_per_cta - 1) / rows_per_cta;
+  p.n_q_tiles = n_q_tiles;
   p.head_offset = heads_begin;
   const float scale = d->scale > 0.f ? d->scale : 1.0f / std::sqrt(static_cast<float>(D));
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -431,6 +446,7 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
   }
   p.status = ctx->d_status;
   p.probe = ctx->score_probe;
+  p.fp32_p = d->numerics == ANIMAXS_NUMERICS_FP32_SCORES_AND_SOFTMAX ? 1 : 0;
   if (peers != nullptr) {
     if (peers->n < 0 || peers->n > ax::kMaxPeers || (d->head_dim != 64 && d->head_dim != 128))
       return ax_set_error(ctx, ANIMAXS_ERR_INVALID_ARG, "peer stores need head_dim 64 or 128 and <= 7 peers");

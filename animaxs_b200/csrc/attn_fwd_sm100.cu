@@ -120,7 +120,9 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint3
   }
 }
 // Half `hf` of O (+)= P V: k-steps 4*hf .. 4*hf+3 (keys [64*hf, 64*hf+64)).
-template <int HD>
+// kFp32P: P is held as P_hi (columns [0, 64) of the S tile) plus P_lo
+// (columns [64, 128)) and both are multiplied into the same accumulator.
+template <int HD, bool kFp32P>
 __device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
                                               int hf, bool accumulate) {
   const uint64_t b0 = vmajor_desc(v_tile, 0);
@@ -129,6 +131,14 @@ __device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, 
     const int kk = hf * 4 + k4;
     umma_f16_ts_warp(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV<HD>,
                 (accumulate || kk > 0) ? 1u : 0u);
+  }
+  if constexpr (kFp32P) {
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+      const int kk = hf * 4 + k4;
+      umma_f16_ts_warp(d_tmem, p_tmem + 64 + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4),
+                       kIdescPV<HD>, 1u);
+    }
   }
 }
 
@@ -140,8 +150,10 @@ __device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, i
 }
 
 // kProbe: also record the scores' numerical health (animaxs_attn_set_score_probe);
-// a separate instantiation so that the production kernel carries no trace of it.
-template <int HD, bool kProbe>
+// kFp32P: the FP32_SCORES_AND_SOFTMAX numerics (exp2 on the SFU only, P x V
+// from P_hi + P_lo).  Separate instantiations, so that the production kernel
+// carries no trace of either.
+template <int HD, bool kProbe, bool kFp32P>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -307,10 +319,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t pph = (tA + j) & 1u;
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 0), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half<HD>(tmem + kColO, tmem + 0, vt, 0, j > 0);
+          issue_pv_half<HD, kFp32P>(tmem + kColO, tmem + 0, vt, 0, j > 0);
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 1), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half<HD>(tmem + kColO, tmem + 0, vt, 1, true);
+          issue_pv_half<HD, kFp32P>(tmem + kColO, tmem + 0, vt, 1, true);
           if (j == nA - 1) tc_commit_warp(BAR(kBarODone + 0));
         }
         if (j1 < n_kv) {
@@ -325,10 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t pph = (tB + j) & 1u;
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 2), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half<HD>(tmem + kColO + HD, tmem + 128, vt, 0, j > 0);
+          issue_pv_half<HD, kFp32P>(tmem + kColO + HD, tmem + 128, vt, 0, j > 0);
           if (!(ok = mbar_wait_warp(BAR(kBarPHalf + 3), pph, abort_flag, p.status))) break;
           tc_fence_after();
-          issue_pv_half<HD>(tmem + kColO + HD, tmem + 128, vt, 1, true);
+          issue_pv_half<HD, kFp32P>(tmem + kColO + HD, tmem + 128, vt, 1, true);
           if (j == nB - 1) tc_commit_warp(BAR(kBarODone + 1));
         }
         // V_j's last reader has been issued: release its stage now (the commit
@@ -472,13 +484,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[2][32];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
+          uint32_t pl[kFp32P ? 32 : 1];
 #pragma unroll
           for (int c = half * 64; c < half * 64 + 64; c += 2) {
             const float2 x = fma2(make_float2(__uint_as_float(s[c >> 5][c & 31]),
                                               __uint_as_float(s[c >> 5][(c + 1) & 31])),
                                   sl2v, nmv);
             float2 pr;
-            if (((c >> 1) & 7) < kPolyPairsPer8) {
+            if (!kFp32P && ((c >> 1) & 7) < kPolyPairsPer8) {
               pr = ex2_poly2(x);
             } else {
               pr.x = ex2_approx(x.x);
@@ -486,10 +499,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], pr);
             pk[half][(c >> 1) & 31] = pack_half2(pr.x, pr.y);
+            if constexpr (kFp32P) {
+              // P_lo = fp16(P - P_hi); the difference is exact in fp32.
+              const float2 hv = __half22float2(*reinterpret_cast<const __half2*>(&pk[half][(c >> 1) & 31]));
+              pl[(c >> 1) & 31] = pack_half2(__fsub_rn(pr.x, hv.x), __fsub_rn(pr.y, hv.y));
+            }
           }
           // Publish this half of P: the MMA warp starts its half of PV_X(j) while
-          // the second half is still being computed.
+          // the second half is still being computed.  (P_lo of keys [64h, 64h+64)
+          // lands in S columns [64+32h, 96+32h), whose scores this thread
+          // already holds in registers.)
           tmem_st32(s_addr + half * 32, pk[half]);
+          if constexpr (kFp32P) tmem_st32(s_addr + 64 + half * 32, pl);
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(BAR(kBarPHalf + 2 * X + half));
@@ -598,12 +619,11 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   cudaError_t e;
   const uint64_t bit = 1ull << (dev & 63);
   if ((configured.load(std::memory_order_acquire) & bit) == 0) {
-    e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Smem<HD>::kBytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               Smem<HD>::kBytes);
-    if (e != cudaSuccess) return e;
+    for (auto fn : {attn_fwd_sm100_kernel<HD, false, false>, attn_fwd_sm100_kernel<HD, true, false>,
+                    attn_fwd_sm100_kernel<HD, false, true>, attn_fwd_sm100_kernel<HD, true, true>}) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<HD>::kBytes);
+      if (e != cudaSuccess) return e;
+    }
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   // Persistent grid: one CTA per SM (at most one per work item).
@@ -626,10 +646,11 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
                    p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
     return cudaErrorInvalidValue;
-  if (q.probe != nullptr)
-    attn_fwd_sm100_kernel<HD, true><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
-  else
-    attn_fwd_sm100_kernel<HD, false><<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
+  auto kernel = q.probe != nullptr ? (q.fp32_p ? attn_fwd_sm100_kernel<HD, true, true>
+                                                : attn_fwd_sm100_kernel<HD, true, false>)
+                                   : (q.fp32_p ? attn_fwd_sm100_kernel<HD, false, true>
+                                               : attn_fwd_sm100_kernel<HD, false, false>);
+  kernel<<<grid, kThreads, Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
   return cudaGetLastError();
 }
 

@@ -31,6 +31,7 @@ struct AttnFwdParams {
   long long o_tok, o_head, o_batch;  // output strides (elements)
   unsigned int* status;  // device status word (bit 0: a bounded wait timed out)
   unsigned int* probe;   // score-health slot uint32[4] (animaxs_attn_set_score_probe) or nullptr
+  int fp32_p;            // FP32_SCORES_AND_SOFTMAX: P x V from fp32 P (hi + lo fp16 terms)
   // Fused head-sharded gather (head dims 64 / 128; n_peers = 0 otherwise): the
   // epilogue also stores every output tile at the same offset in each peer's
   // output (peer GPU memory mapped into this process), and each CTA that

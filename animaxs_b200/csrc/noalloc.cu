@@ -23,9 +23,12 @@
 //  - In host code the array's name is not a device address.  The device
 //    address is looked up once per device with cudaGetSymbolAddress, with that
 //    device current, on the first call made on it; make that first call before
-//    any stream capture.
-//  - No context is involved, so there is no last-error text and device-side
-//    wait timeouts are not reported (the kernels still end on their own).
+//    any stream capture.  The address is kept for the life of the process: after
+//    cudaDeviceReset (or any teardown of the device's primary context) it is
+//    stale, so do not use this entry point across a device reset.
+//  - No context is involved, so there is no last-error text.  A device-side
+//    wait that expires sets a second file-scope word (looked up like the
+//    array), which animaxs_attn_noalloc_status reads and clears.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -40,23 +43,33 @@ namespace {
 constexpr int64_t kNoAllocScratchBytes = int64_t{32} << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+// Timeout bit of the kernels' bounded waits for calls made here.
+static __device__ unsigned int g_noalloc_status;
 
 constexpr int kMaxDevices = 64;
 
-// Device address of g_noalloc_scratch on `dev` (which must be current).
-int scratch_address(int dev, void** out) {
+struct Symbols {
+  void* scratch;
+  unsigned int* status;
+};
+
+// Device addresses of g_noalloc_scratch / g_noalloc_status on `dev` (which
+// must be current), looked up on the first call made on that device.
+int symbol_addresses(int dev, Symbols* out) {
   static std::mutex mu;
-  static void* addr[kMaxDevices] = {};
+  static Symbols addr[kMaxDevices] = {};
   if (dev < 0 || dev >= kMaxDevices) return ANIMAXS_ERR_NO_DEVICE;
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  if (addr[dev].scratch == nullptr) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
+    void* st = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&st, g_noalloc_status);
+    if (e != cudaSuccess || p == nullptr || st == nullptr) {
       cudaGetLastError();
       return ANIMAXS_ERR_CUDA;
     }
-    addr[dev] = p;
+    addr[dev] = Symbols{p, static_cast<unsigned int*>(st)};
   }
   *out = addr[dev];
   return ANIMAXS_OK;
@@ -81,6 +94,9 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
       major != 10 || minor != 0)
     return ANIMAXS_ERR_NO_DEVICE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  Symbols sym{};
+  rc = symbol_addresses(dev, &sym);
+  if (rc != ANIMAXS_OK) return rc;
 
   const int64_t D = d->head_dim;
   const void* qa = q;
@@ -88,12 +104,12 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
   int64_t q_st = d->q_tok_stride, q_sh = d->q_head_stride, q_sb = d->q_batch_stride;
   int64_t k_st = d->k_tok_stride, k_sh = d->k_head_stride, k_sb = d->k_batch_stride;
   if (d->qk_norm != ANIMAXS_QK_NONE) {
-    void* scratch = nullptr;
-    rc = scratch_address(dev, &scratch);
-    if (rc != ANIMAXS_OK) return rc;
-    const int64_t q_bytes = static_cast<int64_t>(d->batch) * d->q_len * d->heads * D * 2;
-    __half* qn = static_cast<__half*>(scratch);
-    __half* kn = reinterpret_cast<__half*>(static_cast<char*>(scratch) +
+    // Layout as animaxs_attn_scratch_bytes counts it: q's copy (when q is
+    // normalised here), then k's at the next 256-byte boundary.
+    const bool q_here = d->qk_norm_targets != ANIMAXS_QK_NORM_K_ONLY;
+    const int64_t q_bytes = q_here ? static_cast<int64_t>(d->batch) * d->q_len * d->heads * D * 2 : 0;
+    __half* qn = static_cast<__half*>(sym.scratch);
+    __half* kn = reinterpret_cast<__half*>(static_cast<char*>(sym.scratch) +
                                            ((q_bytes + 255) & ~static_cast<int64_t>(255)));
     ax::NormParams np{};
     np.head_dim = static_cast<int>(d->head_dim);
@@ -134,6 +150,7 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
     np.njobs = 0;
     if (norm_q) np.job[np.njobs++] = q_job;
     if (norm_k) np.job[np.njobs++] = k_job;
+    np.status = sym.status;
     if (ax::launch_qk_norm(np, stream) != cudaSuccess) return ANIMAXS_ERR_CUDA;
     if (norm_q) {
       qa = qn;
@@ -176,8 +193,23 @@ extern "C" int animaxs_attn_forward_noalloc(const animaxs_attn_desc* d, const vo
   p.o_tok = d->o_tok_stride;
   p.o_head = d->o_head_stride;
   p.o_batch = d->o_batch_stride;
-  p.status = nullptr;
+  p.status = sym.status;
+  p.fp32_p = d->numerics == ANIMAXS_NUMERICS_FP32_SCORES_AND_SOFTMAX ? 1 : 0;
   if (ax::launch_attn_fwd(tq, tk, tv, p, d->heads, d->batch, stream) != cudaSuccess)
     return ANIMAXS_ERR_CUDA;
   return ANIMAXS_OK;
+}
+
+extern "C" int animaxs_attn_noalloc_status(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ANIMAXS_ERR_NO_DEVICE;
+  Symbols sym{};
+  int rc = symbol_addresses(dev, &sym);
+  if (rc != ANIMAXS_OK) return rc;
+  unsigned int status = 0;
+  cudaError_t e = cudaMemcpy(&status, sym.status, sizeof(status), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && status != 0) e = cudaMemset(sym.status, 0, sizeof(status));
+  if (e != cudaSuccess) return ANIMAXS_ERR_CUDA;
+  if (status & ax::kStatusTimeoutBit) return ANIMAXS_ERR_TIMEOUT;
+  return status != 0 ? ANIMAXS_ERR_CUDA : ANIMAXS_OK;
 }

@@ -33,6 +33,9 @@ from ._lib import (AttentionValidationError, AttnDesc, QK_NONE, QK_RMS, QK_RMS_R
                    raise_for)
 
 NUMERICS = ("legacy", "fp32ScoresAndSoftmax", "bf16_compute")
+# animaxs_numerics
+_NUMERICS = {"legacy": _lib.NUMERICS_LEGACY, "fp32ScoresAndSoftmax": _lib.NUMERICS_FP32,
+             "bf16_compute": _lib.NUMERICS_BF16}
 BACKENDS = ("legacyHeadMajorMPS", "stridedTokenMajorMPS", "streamingMPS", "metalFlash")
 _QK = {"none": QK_NONE, "rms": QK_RMS, "rms_rope": QK_RMS_ROPE}
 # animaxs_qk_norm_targets: which of q and k the qk_norm mode applies to.
@@ -195,6 +198,7 @@ class AttentionExecutor:
         d = AttnDesc()
         self._lib.animaxs_attn_desc_init(ctypes.byref(d), batch, heads, kv_heads, query_count,
                                          key_count, head_dim)
+        d.numerics = _NUMERICS[self.numerics]
         if layout.is_token_major:
             ts = layout.token_stride
             d.q_tok_stride = d.o_tok_stride = ts

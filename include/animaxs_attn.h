@@ -39,8 +39,10 @@ extern "C" {
 #endif
 
 /* 2: animaxs_proj_desc gained the weight-storage fields (w_storage, w_scale,
- * w_zero, w_packed_stride); the peer-group and dequant entry points. */
-#define ANIMAXS_ATTN_ABI_VERSION 2
+ * w_zero, w_packed_stride); the peer-group and dequant entry points.
+ * 3: animaxs_attn_desc gained `numerics`; the cross-K/V cache and the
+ * no-alloc status entry points. */
+#define ANIMAXS_ATTN_ABI_VERSION 3
 
 /* Status codes.  The reference throws AnimapkError.validation(String) for every
  * argument problem (AttentionExecutor.swift:778-825) and surfaces GPU errors as
@@ -84,6 +86,27 @@ typedef enum animaxs_qk_norm_targets {
   ANIMAXS_QK_NORM_K_ONLY = 2
 } animaxs_qk_norm_targets;
 
+/* Arithmetic of the attention (`numerics:` of AttentionExecutor.init,
+ * AttentionExecutor.swift:97-110).
+ *  LEGACY  - fp32 scores (fp16 q.k products summed in fp32) and fp32 softmax
+ *            statistics; the probabilities are rounded to fp16 for the P x V
+ *            product (the reference's legacy path also rounds the scores).
+ *  FP32_SCORES_AND_SOFTMAX - the reference's diagnostic mode (encodeFP32,
+ *            AttentionExecutor.swift:325-405; kernels attention_qk_f16_to_f32,
+ *            attention_softmax_rows_f32, attention_pv_f32_f16_to_f16,
+ *            AnimaKernels.metal:1105-1185): fp32 scores, fp32 softmax and
+ *            fp32 probabilities times fp16 V with fp32 accumulation.  Here P
+ *            enters the tensor-core product as two fp16 terms, P_hi = fp16(P)
+ *            and P_lo = fp16(P - P_hi), which together carry ~22 significant
+ *            bits, and exp2 is evaluated on the SFU only.  About 1.3x the time
+ *            of LEGACY.  Head dims 64 and 128.
+ *  BF16_COMPUTE - an Apple5 bf16 rounding emulation: ANIMAXS_ERR_UNSUPPORTED. */
+typedef enum animaxs_numerics {
+  ANIMAXS_NUMERICS_LEGACY = 0,
+  ANIMAXS_NUMERICS_FP32_SCORES_AND_SOFTMAX = 1,
+  ANIMAXS_NUMERICS_BF16_COMPUTE = 2
+} animaxs_numerics;
+
 /* One attention call.  Replaces the argument list of
  * AttentionExecutor.encode(commandBuffer:query:queryOffset:key:...:heads:
  * queryCount:keyCount:headDim:keyValueHeads:causal:probe:layout:)
@@ -121,6 +144,7 @@ typedef struct animaxs_attn_desc {
   /* Optional extents (bytes from the pointer passed to the call) used for the
    * reference's range validation (:808-823); 0 = not checked. */
   int64_t q_bytes, k_bytes, v_bytes, o_bytes;
+  int32_t numerics;          /* animaxs_numerics; 0 = LEGACY */
 } animaxs_attn_desc;
 
 typedef struct animaxs_attn_ctx animaxs_attn_ctx;
@@ -164,10 +188,15 @@ int animaxs_attn_forward(animaxs_attn_ctx* ctx, const animaxs_attn_desc* desc,
  * which awaits the command buffer and rethrows `completed.error`. */
 int animaxs_attn_synchronize(animaxs_attn_ctx* ctx, void* stream);
 
-/* Scratch bytes a call with `desc` needs (the fused q/k normalisation writes
- * normalised copies).  Replaces maximumScoreScratchBytes(keyCount:queryCount:)
- * (AttentionExecutor.swift:112-120); the flash kernel itself needs no score scratch. */
+/* Scratch bytes the fused q/k normalisation of a call with `desc` needs when
+ * it runs as a prologue: the normalised copy of q (unless qk_norm_targets is
+ * K_ONLY) and, at the next 256-byte boundary, of k (unless Q_ONLY); 0 for
+ * qk_norm NONE; animaxs_attn_forward's context scratch and
+ * animaxs_attn_forward_noalloc's fixed array hold exactly this.  Replaces
+ * maximumScoreScratchBytes(keyCount:queryCount:) (AttentionExecutor.swift:112-120);
+ * the flash kernel itself needs no score scratch. */
 int animaxs_attn_scratch_bytes(const animaxs_attn_desc* desc, int64_t* bytes);
+
 
 /* Number of (head, 128-row query tile) units executed on this context since
  * creation; the counter the reference keeps with
@@ -226,6 +255,64 @@ int animaxs_rmsnorm_heads_half(animaxs_attn_ctx* ctx, const void* in, void* out,
                                const void* weight, int tokens, int heads, int head_dim,
                                int64_t row_stride, float eps, void* stream);
 
+/* ---- Cross-attention K/V cache ---------------------------------------------
+ * Replaces CrossKVCache (DiTBlockExecutor.swift:19-43) and its use by the DiT
+ * block (:1105-1161): the cross-attention K and V of every block depend only
+ * on the LLM-adapter context, so they are projected (and K RMS-normalised)
+ * once per generation and reused by the other Euler steps.  A cache holds
+ * `blocks` blocks of [batch][tokens][K | V] fp16 rows: a token's row is its
+ * kv_heads x head_dim K values followed by its kv_heads x head_dim V values
+ * (token stride 2 x kv_heads x head_dim elements).  Attention reads a block in
+ * place: pass the pointers and strides from animaxs_cross_kv_cache_block as k
+ * and v with qk_norm RMS and qk_norm_targets Q_ONLY (the reference blits a hit
+ * back into its scratch instead).  Like the reference's cache it belongs to
+ * one generation; animaxs_cross_kv_cache_reset starts the next.  Not
+ * reentrant; work is enqueued on `stream`. */
+typedef struct animaxs_cross_kv_cache animaxs_cross_kv_cache;
+
+/* Device bytes of a cache (CrossKVCache.blockStride x blockCount). */
+int animaxs_cross_kv_cache_bytes(int blocks, int batch, int tokens, int kv_heads, int head_dim,
+                                 int64_t* bytes);
+
+/* A cache on ctx's device (head_dim 64 or 128).  `memory` (256-byte aligned,
+ * >= animaxs_cross_kv_cache_bytes) is used if given, else the cache allocates
+ * its own (CrossKVCache.init, :30-36); the cache keeps `ctx` for errors and launches. */
+int animaxs_cross_kv_cache_create(animaxs_attn_ctx* ctx, int blocks, int batch, int tokens, int kv_heads,
+                                  int head_dim, void* memory, int64_t memory_bytes,
+                                  animaxs_cross_kv_cache** out);
+int animaxs_cross_kv_cache_destroy(animaxs_cross_kv_cache* cache);
+
+/* Store block `block` from projected K and V ([batch][tokens][kv_heads x
+ * head_dim] fp16, token / batch strides in elements).  With k_norm = 1, K is
+ * RMS-normalised with `k_norm_weight` (fp16[head_dim] or NULL) by the same
+ * kernel as the attention prologue, so attention on the cached block equals
+ * the uncached fused call bit for bit; k_norm = 0 stores K as given.  Marks
+ * the block ready (the miss path of :1123-1160: project, RMSNorm K, store). */
+int animaxs_cross_kv_cache_fill(animaxs_cross_kv_cache* cache, int block, const void* k, int64_t k_tok_stride,
+                                int64_t k_batch_stride, const void* v, int64_t v_tok_stride,
+                                int64_t v_batch_stride, int k_norm, const void* k_norm_weight, float eps,
+                                void* stream);
+
+/* Store block `block` straight from the adapter context: one fused projection
+ * of `context` ([batch x tokens][context_dim] fp16, rows context_stride
+ * elements apart) against `w_kv` ([2 x kv_heads x 128][context_dim]: the
+ * cross W_k rows, then the cross W_v rows; rows w_stride apart), the
+ * projection rounded to fp16 and the K columns RMS-normalised in the
+ * epilogue (animaxs_proj_forward with ANIMAXS_PROJ_QKV_NORM).  head_dim 128.
+ * Marks the block ready. */
+int animaxs_cross_kv_cache_project(animaxs_cross_kv_cache* cache, int block, const void* context,
+                                   int64_t context_stride, int context_dim, const void* w_kv, int64_t w_stride,
+                                   const void* k_norm_weight, float eps, void* stream);
+
+/* Block `block`'s K and V device pointers, token and batch strides (elements)
+ * and whether it is ready (CrossKVCache.kOffset / vOffset / isReady, :38-41). */
+int animaxs_cross_kv_cache_block(const animaxs_cross_kv_cache* cache, int block, void** k, void** v,
+                                 int64_t* tok_stride, int64_t* batch_stride, int* ready);
+/* CrossKVCache.markReady (:42) for a block the caller filled itself; reset
+ * marks every block not ready. */
+int animaxs_cross_kv_cache_mark_ready(animaxs_cross_kv_cache* cache, int block, int ready);
+int animaxs_cross_kv_cache_reset(animaxs_cross_kv_cache* cache);
+
 /* Host helpers (no GPU).  DiT 3-D RoPE table [T*H*W][64][2][2] fp32 with the
  * t/h/w = 44/42/42 dim split, theta_hw = 10000*4^(42/40), theta_t = 1e4.
  * Replaces DitRoPE.generate(T:H:W:) (DitRoPE.swift:58-107).  `out` holds
@@ -260,11 +347,21 @@ int animaxs_gqa_kv_head(int query_head, int heads, int kv_heads);
  *    contents (every byte read is rewritten first); calls that overlap on the
  *    GPU race on it, so serialise them.
  *  - The first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress); make that call before any stream capture.
- *  - Returns status codes only (no last-error text); device-side wait
- *    timeouts are not reported. */
+ *    (cudaGetSymbolAddress); make that call before any stream capture.  The
+ *    address is kept for the life of the process, so it goes stale after
+ *    cudaDeviceReset: do not use this entry point across a device reset.
+ *  - Returns status codes only (no last-error text).  A bounded device-side
+ *    wait that expires is recorded in a fixed device word of the current
+ *    device, read with animaxs_attn_noalloc_status. */
 int animaxs_attn_forward_noalloc(const animaxs_attn_desc* desc, const void* q, const void* k,
                                  const void* v, void* o, void* stream);
+
+/* Read and clear the current device's status word of
+ * animaxs_attn_forward_noalloc: ANIMAXS_ERR_TIMEOUT when a bounded
+ * device-side wait of one of its calls expired since the last read, else
+ * ANIMAXS_OK.  Synchronise the streams of the calls it should cover first.
+ * Allocates nothing. */
+int animaxs_attn_noalloc_status(void);
 
 /* Failure-detection self-test: enqueue one kernel whose only thread waits,
  * through the same bounded device-side wait every kernel here uses, on a

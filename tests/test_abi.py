@@ -115,6 +115,13 @@ def test_validation_mirrors_reference(lib):
     assert _validate(lib, _desc(lib, qk_norm=7)) == -1
     # overflow
     assert _validate(lib, _desc(lib, q_batch_stride=1 << 45, batch=2)) == -8
+    # numerics (AttentionExecutor.init numerics:): legacy and fp32ScoresAndSoftmax run at
+    # head_dim 64 / 128; bf16Compute is not built; fp32 on the wide-head kernel is not built
+    assert _validate(lib, _desc(lib, numerics=1)) == 0
+    assert _validate(lib, _desc(lib, numerics=1, head_dim=64)) == 0
+    assert _validate(lib, _desc(lib, numerics=2)) == -2
+    assert _validate(lib, _desc(lib, numerics=3)) == -1
+    assert _validate(lib, _desc(lib, numerics=1, heads=1, kv_heads=1, head_dim=384)) == -2
 
 
 def test_scratch_bytes(lib):
@@ -122,9 +129,21 @@ def test_scratch_bytes(lib):
     n = ctypes.c_int64()
     assert lib.animaxs_attn_scratch_bytes(ctypes.byref(d), ctypes.byref(n)) == 0
     assert n.value == 4096 * 16 * 256 + 512 * 16 * 256
+    # only the copies the prologue writes: q only (k cached by the caller), k only
+    d.qk_norm_targets = 1
+    lib.animaxs_attn_scratch_bytes(ctypes.byref(d), ctypes.byref(n))
+    assert n.value == 4096 * 16 * 256
+    d.qk_norm_targets = 2
+    lib.animaxs_attn_scratch_bytes(ctypes.byref(d), ctypes.byref(n))
+    assert n.value == 512 * 16 * 256
     d.qk_norm = 0
     lib.animaxs_attn_scratch_bytes(ctypes.byref(d), ctypes.byref(n))
     assert n.value == 0
+
+
+def test_noalloc_status_without_gpu(lib):
+    """The no-alloc status query fails cleanly without a device (it never allocates)."""
+    assert lib.animaxs_attn_noalloc_status() in (-6, -4)
 
 
 @pytest.mark.parametrize("grid", [(1, 32, 32), (1, 64, 64), (2, 8, 12)])
