@@ -4,8 +4,8 @@ The product is ``libanimaxs_attn.so`` (C ABI, ``include/animaxs_attn.h``); this
 package holds its CUDA sources (``csrc/``), the in-tree build
 (``build.py``) and the host-side mirror of the reference's Swift
 ``AttentionExecutor`` interface (``executor.py``), plus the fused attention
-projections (``projection.py``) and the cross-attention K/V cache
-(``cross_kv_cache.py``).
+projections (``projection.py``), the cross-attention K/V cache
+(``cross_kv_cache.py``) and the weight streamer (``weight_streamer.py``).
 """
 
 from ._lib import (AttentionDeviceError, AttentionError, AttentionTimeoutError,  # noqa: F401
@@ -15,3 +15,4 @@ from .executor import (AttentionExecutor, AttentionInputLayout, DeviceBuffer,  #
 from .projection import ProjectionExecutor, QuantizedWeight  # noqa: F401,E402
 from .probe import ProbeStats, ScoreProbe  # noqa: F401,E402
 from .cross_kv_cache import CrossKVCache  # noqa: F401,E402
+from .weight_streamer import WeightStreamer  # noqa: F401,E402

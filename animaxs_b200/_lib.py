@@ -138,6 +138,15 @@ SIGNATURES = {
                                           ctypes.POINTER(_I64), ctypes.POINTER(_I)]),
     "animaxs_cross_kv_cache_mark_ready": (_I, [_P, _I, _I]),
     "animaxs_cross_kv_cache_reset": (_I, [_P]),
+    "animaxs_weight_streamer_create": (_I, [_P, _I64, _I, ctypes.POINTER(_P)]),
+    "animaxs_weight_streamer_destroy": (_I, [_P]),
+    "animaxs_weight_streamer_register_host": (_I, [_P, _P, _I64]),
+    "animaxs_weight_streamer_load": (_I, [_P, _I, _P, _I64, _I64, _P]),
+    "animaxs_weight_streamer_slot": (_P, [_P, _I]),
+    "animaxs_weight_streamer_wait_loaded": (_I, [_P, _I, _P]),
+    "animaxs_weight_streamer_mark_in_flight": (_I, [_P, _I, _P]),
+    "animaxs_weight_streamer_complete": (_I, [_P, _I]),
+    "animaxs_weight_streamer_state": (_I, [_P, _I, ctypes.POINTER(_I64), ctypes.POINTER(_I)]),
     "animaxs_proj_desc_init": (_I, [ctypes.POINTER(ProjDesc), _I, _I, _I, _I]),
     "animaxs_proj_validate": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P]),
     "animaxs_proj_forward": (_I, [_P, ctypes.POINTER(ProjDesc), _P, _P, _P, _P]),

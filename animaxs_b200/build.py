@@ -20,7 +20,7 @@ LIB = os.path.join(HERE, "libanimaxs_attn.so")
 CALL_BENCH = os.path.join(BUILD, "call_bench")
 SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "attn_wide_sm100.cu", "qk_norm.cu", "sharded.cu",
            "noalloc.cu", "proj_api.cu", "proj_sm100.cu", "dequant_sm100.cu",
-           "peer_sync.cu", "peer_sharded.cu", "cross_kv_cache.cu"]
+           "peer_sync.cu", "peer_sharded.cu", "cross_kv_cache.cu", "weight_streamer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
          "--expt-relaxed-constexpr", "-Xptxas", "-v"]

@@ -57,6 +57,8 @@ struct AxPeers {
   int n;
   long long delta[7];
   unsigned int* arrive[7];
+  const unsigned int* go;  // the stores and arrivals happen only if *go == go_value
+  unsigned int go_value;
 };
 int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const void* q,
                      const void* k, const void* v, void* o, int heads_begin, int heads_count,

@@ -455,6 +455,8 @@ int ax_forward_range(animaxs_attn_ctx* ctx, const animaxs_attn_desc* d, const vo
       p.peer_delta[i] = peers->delta[i];
       p.peer_arrive[i] = peers->arrive[i];
     }
+    p.peer_go = peers->go;
+    p.peer_go_value = peers->go_value;
   }
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
   if (ctx->timing) {

@@ -197,6 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   const int w0 = static_cast<int>(blockIdx.x);
   const int wstep = static_cast<int>(gridDim.x);
+  // Fused gather: store into the peers only after a completed handshake.
+  const bool peers_go = p.n_peers > 0 && (p.peer_go == nullptr || *p.peer_go == p.peer_go_value);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
@@ -556,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            I.q0 + X * kTileM + (warp & 3) * 32, I.h - p.o_head_base, I.b);
               tma_store_commit();
             }
-            if (p.n_peers > 0) {
+            if (peers_go) {
               // Fused head-sharded gather: the same 32 x 64 tile to the same
               // place in every peer's output over NVLink, 8 lanes per row
               // (128 contiguous bytes), 4 rows per step.  The stage is only
@@ -587,14 +589,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (warp < 8 && lane == 0) tma_store_wait_all();  // the output stores have completed
-  if (p.n_peers > 0 && warp < 8) __threadfence_system();  // peer stores before the arrival below
+  if (peers_go && warp < 8) __threadfence_system();  // peer stores before the arrival below
   tc_fence_before();
   __syncthreads();
   if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-  if (p.n_peers > 0 && threadIdx.x == 0 && *abort_flag == 0) {
+  if (peers_go && threadIdx.x == 0 && *abort_flag == 0) {
     // This CTA's items are in every peer's output: count them on each peer's
     // arrival word for this rank (a CTA that timed out does not arrive, so the
     // peers' waits report the failure instead of reading a partial output).

@@ -40,6 +40,10 @@ struct AttnFwdParams {
   int n_peers;
   long long peer_delta[7];           // bytes from `o` to the peer's copy of it
   unsigned int* peer_arrive[7];      // the peer's arrival word for this rank
+  // The peer stores and arrivals happen only if *peer_go == peer_go_value:
+  // the handshake before the call writes it when every peer was ready.
+  const unsigned int* peer_go;
+  unsigned int peer_go_value;
 };
 
 constexpr int kMaxPeers = 7;  // 8 GPUs per node
@@ -87,7 +91,8 @@ cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
 // Peer handshake of the fused head-sharded path (peer_sync.cu): one block adds
 // `add` to each peer's word `signal[i]` (release, system scope), then waits
 // until every own word `wait[i]` (i != rank) has reached `target` (acquire,
-// system scope; bounded by timeout_ns, after which kStatusTimeoutBit is set).
+// system scope; bounded by timeout_ns, after which kStatusTimeoutBit is set)
+// and, if no wait gave up, writes `go_value` to `go`.
 struct PeerSyncParams {
   unsigned int* signal[8];   // peers' words for this rank (mapped here); nullptr: no signal
   unsigned int add;
@@ -96,6 +101,8 @@ struct PeerSyncParams {
   int world, rank;
   unsigned long long timeout_ns;
   unsigned int* status;
+  unsigned int* go;          // set to go_value when every wait succeeded (nullptr: not written)
+  unsigned int go_value;
 };
 cudaError_t launch_peer_sync(const PeerSyncParams& p, cudaStream_t stream);
 

@@ -10,11 +10,13 @@
 //   1. peer_sync: add 1 to every peer's "ready" word for r, wait until every
 //      peer's "ready" word here reached the call number (each peer has
 //      reached this call in its stream, so it is done with the previous
-//      output), bounded;
+//      output), bounded; only if every peer was ready, write the call number
+//      to this rank's "go" word;
 //   2. the attention kernel for heads [r*H/W, (r+1)*H/W): its epilogue stores
-//      each output tile locally (TMA) and at the same offset in every peer's
-//      buffer (NVLink stores), and every CTA adds its item count to every
-//      peer's "arrive" word for r (release, system scope);
+//      each output tile locally (TMA) and, if the "go" word holds this call's
+//      number, at the same offset in every peer's buffer (NVLink stores), and
+//      every CTA then adds its item count to every peer's "arrive" word for r
+//      (release, system scope);
 //   3. peer_sync: wait until every peer's "arrive" word here reached
 //      call number x items per rank, bounded.
 // After step 3 the local buffer holds every rank's heads.
@@ -34,9 +36,10 @@
 namespace {
 
 constexpr int kMaxWorld = 8;
-constexpr int64_t kFlagBytes = 256;  // ready [0, 8), arrive [8, 16) (uint32)
+constexpr int64_t kFlagBytes = 256;  // ready [0, 8), arrive [8, 16), go [16] (uint32)
 constexpr int kReady = 0;
 constexpr int kArrive = 8;
+constexpr int kGo = 16;  // written by this rank's ready handshake only
 
 }  // namespace
 
@@ -224,6 +227,8 @@ extern "C" int animaxs_attn_forward_head_sharded_peer(animaxs_attn_ctx* ctx, ani
   ready.rank = rank;
   ready.timeout_ns = ANIMAXS_WAIT_TIMEOUT_NS;
   ready.status = ctx->d_status;
+  ready.go = flags_of(g, rank) + kGo;
+  ready.go_value = call;
   cudaError_t e = ax::launch_peer_sync(ready, stream);
   if (e != cudaSuccess) return ax_cuda_fail(ctx, e, "peer handshake launch");
 
@@ -234,6 +239,11 @@ extern "C" int animaxs_attn_forward_head_sharded_peer(animaxs_attn_ctx* ctx, ani
     peers.arrive[peers.n] = flags_of(g, r) + kArrive + rank;
     ++peers.n;
   }
+  // A peer that was not ready (the handshake gave up) may still be reading its
+  // previous output: then the kernel stores nothing into any peer and adds no
+  // arrivals, so the peers' closing waits report the failure too.
+  peers.go = flags_of(g, rank) + kGo;
+  peers.go_value = call;
   rc = ax_forward_range(ctx, d, q, k, v, o, h0, hr, nullptr, stream, &peers);
   if (rc != ANIMAXS_OK) return rc;
 

@@ -8,7 +8,8 @@
 // words only grow; "reached" is a wrap-safe signed difference.  Every wait is
 // bounded by `timeout_ns` of %globaltimer, after which the status word gets
 // the timeout bit and the kernel returns: a peer that never arrives cannot
-// hang this GPU.
+// hang this GPU.  When every wait succeeded it writes the call's "go" value,
+// without which the attention kernel that follows stores nothing into a peer.
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -24,16 +25,21 @@ __global__ void __launch_bounds__(32) peer_sync_kernel(const PeerSyncParams p) {
     for (int r = 0; r < p.world; ++r)
       if (r != p.rank && p.signal[r] != nullptr) red_add_release_sys(p.signal[r], p.add);
   }
+  bool ok = true;
   if (i < p.world && i != p.rank) {
     const uint64_t t0 = globaltimer_ns();
     while (static_cast<int>(ld_acquire_sys(p.wait + i) - p.target) < 0) {
       if (globaltimer_ns() - t0 > p.timeout_ns) {
         atomicOr(p.status, kStatusTimeoutBit);
+        ok = false;
         break;
       }
       __nanosleep(200);
     }
   }
+  // Only a handshake that every peer completed lets the next kernel in the
+  // stream write into the peers (it compares the word with this call's value).
+  if (__all_sync(0xffffffffu, ok) && i == 0 && p.go != nullptr) *p.go = p.go_value;
   __syncwarp();
 }
 

@@ -156,6 +156,9 @@ class PeerShardedAttention:
             self.output = torch.as_tensor(_DeviceArray(ptr, self.shape), device=dev)
 
     def close(self):
+        """Free the group.  Every rank must be past its last call first --
+        synchronised, then a barrier across the ranks (``dist.barrier()``) --
+        because a slower peer may still be storing into this rank's buffer."""
         if getattr(self, "_group", None):
             self.output = None
             _lib.lib().animaxs_peer_group_destroy(self._group)

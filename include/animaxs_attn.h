@@ -40,8 +40,8 @@ extern "C" {
 
 /* 2: animaxs_proj_desc gained the weight-storage fields (w_storage, w_scale,
  * w_zero, w_packed_stride); the peer-group and dequant entry points.
- * 3: animaxs_attn_desc gained `numerics`; the cross-K/V cache and the
- * no-alloc status entry points. */
+ * 3: animaxs_attn_desc gained `numerics`; the cross-K/V cache, weight
+ * streamer and no-alloc status entry points. */
 #define ANIMAXS_ATTN_ABI_VERSION 3
 
 /* Status codes.  The reference throws AnimapkError.validation(String) for every
@@ -313,6 +313,46 @@ int animaxs_cross_kv_cache_block(const animaxs_cross_kv_cache* cache, int block,
 int animaxs_cross_kv_cache_mark_ready(animaxs_cross_kv_cache* cache, int block, int ready);
 int animaxs_cross_kv_cache_reset(animaxs_cross_kv_cache* cache);
 
+/* ---- Weight streaming --------------------------------------------------------
+ * Replaces WeightStreamer (WeightStreamer.swift:84-213): bounded device memory
+ * of 1 to 4 slots of `capacity` bytes, each loaded with one execution range of
+ * a weight pack (the W8/W4 codes, scales and zeros of a block, as the
+ * reference's .animapk ranges) from host memory, and never overwritten while
+ * queued work still reads it.  The reference copies with the CPU and
+ * ping-pongs two slots so that block n+1's copy overlaps block n's GPU work
+ * (DiTBlockExecutor.swift:222-260); here a load is an asynchronous
+ * host-to-device copy on the caller's stream (use a copy stream to overlap),
+ * and the ordering is kept on the GPU with events:
+ *  - load: copies `bytes` from host `src` into `slot` on `stream` and records
+ *    the slot's "loaded" event; if the slot was marked in flight, the copy
+ *    first waits (on the GPU) for that mark, so in-flight readers always see
+ *    the old contents.  Ranges larger than the slot are refused ("execution
+ *    range does not fit the weight slot").
+ *  - wait_loaded: `consumer_stream` waits (on the GPU) for the slot's last load.
+ *  - mark_in_flight: records that work queued on `consumer_stream` reads the
+ *    slot (markInFlight); complete clears the mark when the caller knows that
+ *    work has finished (complete).
+ *  - register_host: pins a host range (cudaHostRegister, read-only), e.g. the
+ *    mapped pack file, so its loads run as DMA at PCIe speed; undone at destroy.
+ * The slots hold whatever the caller loads; animaxs_proj_forward reads W8/W4
+ * weights straight from a slot (w, w_scale, w_zero point into it). */
+typedef struct animaxs_weight_streamer animaxs_weight_streamer;
+int animaxs_weight_streamer_create(animaxs_attn_ctx* ctx, int64_t capacity, int slots,
+                                   animaxs_weight_streamer** out);
+int animaxs_weight_streamer_destroy(animaxs_weight_streamer* streamer);
+int animaxs_weight_streamer_register_host(animaxs_weight_streamer* streamer, void* base, int64_t bytes);
+int animaxs_weight_streamer_load(animaxs_weight_streamer* streamer, int slot, const void* src, int64_t bytes,
+                                 int64_t logical_index, void* stream);
+/* Device address of `slot` (256-byte aligned), NULL for a bad slot. */
+void* animaxs_weight_streamer_slot(const animaxs_weight_streamer* streamer, int slot);
+int animaxs_weight_streamer_wait_loaded(animaxs_weight_streamer* streamer, int slot, void* consumer_stream);
+int animaxs_weight_streamer_mark_in_flight(animaxs_weight_streamer* streamer, int slot, void* consumer_stream);
+int animaxs_weight_streamer_complete(animaxs_weight_streamer* streamer, int slot);
+/* The logical index of the slot's last load (-1: none) and whether it is
+ * marked in flight (loadedLogicalIndexes / inFlightSlotSet). */
+int animaxs_weight_streamer_state(animaxs_weight_streamer* streamer, int slot, int64_t* logical_index,
+                                  int* in_flight);
+
 /* Host helpers (no GPU).  DiT 3-D RoPE table [T*H*W][64][2][2] fp32 with the
  * t/h/w = 44/42/42 dim split, theta_hw = 10000*4^(42/40), theta_t = 1e4.
  * Replaces DitRoPE.generate(T:H:W:) (DitRoPE.swift:58-107).  `out` holds
@@ -486,7 +526,14 @@ int animaxs_attn_forward_head_sharded(animaxs_attn_ctx* ctx, animaxs_comm* comm,
  * in the same order (like a collective); the output stays valid until this
  * rank's next call.  A peer that does not arrive within ANIMAXS_WAIT_TIMEOUT
  * (2 s) makes animaxs_attn_synchronize report ANIMAXS_ERR_TIMEOUT; the group
- * must then be destroyed and recreated. */
+ * must then be destroyed and recreated.  A call whose opening handshake timed
+ * out stores nothing into any peer (a peer that was not seen ready may still
+ * be reading its previous output) and adds no arrivals, so the peers' own
+ * closing waits report the failure as well.
+ * Teardown: every rank must be past its last call -- synchronised, and then a
+ * barrier across the ranks -- before any rank calls animaxs_peer_group_destroy,
+ * because destroy frees this rank's buffer, into which a slower peer may still
+ * be storing. */
 typedef struct animaxs_peer_group animaxs_peer_group;
 
 int animaxs_peer_group_create(animaxs_attn_ctx* ctx, int world, int rank, int64_t output_bytes,

@@ -141,6 +141,20 @@ def test_scratch_bytes(lib):
     assert n.value == 0
 
 
+def test_cache_and_streamer_need_a_context(lib):
+    """The cross-K/V cache and weight streamer entry points reject a missing
+    context / handle before touching a device."""
+    h = ctypes.c_void_p()
+    assert lib.animaxs_cross_kv_cache_create(None, 28, 1, 512, 16, 128, None, 0, ctypes.byref(h)) == -1
+    assert lib.animaxs_weight_streamer_create(None, 1024, 2, ctypes.byref(h)) == -1
+    assert lib.animaxs_weight_streamer_slot(None, 0) is None
+    assert lib.animaxs_cross_kv_cache_reset(None) == -1
+    n = ctypes.c_int64()
+    assert lib.animaxs_cross_kv_cache_bytes(28, 1, 512, 16, 128, ctypes.byref(n)) == 0
+    assert n.value == 28 * 512 * 2 * 2048 * 2      # CrossKVCache: 28 x 4 MiB
+    assert lib.animaxs_cross_kv_cache_bytes(28, 1, 512, 16, 96, ctypes.byref(n)) == -2
+
+
 def test_noalloc_status_without_gpu(lib):
     """The no-alloc status query fails cleanly without a device (it never allocates)."""
     assert lib.animaxs_attn_noalloc_status() in (-6, -4)

@@ -257,6 +257,12 @@ def _peer_absent_worker(rank, world, port, out):
                             world_size=world)
     ex = ax.AttentionExecutor(rank)
     ps = PeerShardedAttention(ex, rank, world, (1, 512, 16, 128))
+    if rank == 1:
+        # A sentinel in rank 1's output: rank 0's call must not store into a
+        # peer whose readiness it never saw.
+        ps.output.fill_(7.0)
+        torch.cuda.synchronize()
+    dist.barrier()
     if rank == 0:
         # Rank 1 stays alive but never calls: both bounded waits of this call
         # give up (2 s each) and the status word reports the timeout.
@@ -273,6 +279,9 @@ def _peer_absent_worker(rank, world, port, out):
         ex.synchronize()
         out["after"] = bool(torch.isfinite(ref.float()).all())
     dist.barrier()   # rank 1 leaves only after rank 0's kernels have finished
+    if rank == 1:
+        torch.cuda.synchronize()
+        out["untouched"] = bool((ps.output == 7.0).all())
     ps.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -288,6 +297,7 @@ def test_peer_that_never_calls_times_out():
     out = mgr.dict()
     mp.spawn(_peer_absent_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     assert out[0] == "timeout" and out["after"]
+    assert out["untouched"], "rank 0 stored into rank 1's output after its ready handshake timed out"
 
 
 def test_peer_sharded_rejects_bad_shape_before_touching_a_device():
