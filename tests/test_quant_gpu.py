@@ -59,6 +59,9 @@ def _close_fp16(got, want, what):
     bad = err > 2e-3 + 2e-3 * np.abs(want16)
     assert np.all(np.isfinite(got)), f"{what}: non-finite output"
     assert not bad.any(), f"{what}: {bad.sum()} elements out of tolerance, worst {err.max():.3e}"
+    # mean error under a quarter fp16 ulp of the mean magnitude: no systematic bias
+    mean_bound = 2.0 ** -13 * float(np.abs(want16).mean()) + 1e-6
+    assert err.mean() <= mean_bound, f"{what}: mean-abs {err.mean():.3e} > {mean_bound:.3e}"
 
 
 def test_golden_decode(pj):
