@@ -186,12 +186,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     it.h = p.head_offset + hb % p.heads_in_launch;
     it.b = hb / p.heads_in_launch;
     it.kvh = it.h / p.heads_per_kv;
-    it.q0 = pair * 2 * kTileM;
+    // Single-tile items (p.single_tiles): one 128-row tile, processed as tile A.
+    it.q0 = pair * (p.single_tiles ? kTileM : 2 * kTileM);
     int valid = p.kv_valid;
     if (p.kv_valid_dev != nullptr) valid = p.kv_valid_dev[it.b];
     it.valid = min(max(valid, 1), p.kv_len);
     it.nA = kv_tiles_for(it.q0, p.q_len, it.valid, p.causal);
-    it.nB = kv_tiles_for(it.q0 + kTileM, p.q_len, it.valid, p.causal);
+    it.nB = p.single_tiles ? 0 : kv_tiles_for(it.q0 + kTileM, p.q_len, it.valid, p.causal);
     it.n_kv = max(it.nA, it.nB);
     return it;
   };
@@ -253,9 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it > 0 && !(ok = mbar_wait(BAR(kBarQFree), static_cast<uint32_t>((it - 1) & 1),
                                        abort_flag, p.status)))
           break;
-        mbar_arrive_expect_tx(BAR(kBarQ), 2 * kTileBytes);
-#pragma unroll
-        for (int x = 0; x < 2; ++x)
+        // Q_B only when tile B has work (it is never read otherwise).
+        const int qt = I.nB > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(BAR(kBarQ), qt * kTileBytes);
+        for (int x = 0; x < qt; ++x)
 #pragma unroll
           for (int c = 0; c < HD / 64; ++c)
             tma_load_4d(sQ + x * kTileBytes + c * kPanelBytes, &tm_q, BAR(kBarQ), 64 * c,
@@ -612,6 +614,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int attn_fwd_rows_per_cta() { return 2 * kTileM; }
 
+// Work items of a launch.  An item is normally a pair of 128-row query tiles
+// sharing one K/V stream; when the pairs would leave more than half of the SMs
+// idle, items are single tiles (the second softmax warpgroup then idles):
+// twice the CTAs, each ~30 % slower per key tile (its softmax runs with one
+// warp per sub-partition and nothing else to overlap), so the launch finishes
+// sooner.  Every row's arithmetic is the same in both forms, so the output
+// is bit-identical.
+static bool single_tile_items(int q_len, int heads_in_launch, int batch, int sms) {
+  const long long pairs = (q_len + 2 * kTileM - 1) / (2 * kTileM);
+  return 2 * pairs * heads_in_launch * batch <= sms;
+}
+long long attn_fwd_work_items(int q_len, int heads_in_launch, int batch, int sms) {
+  const int rows = single_tile_items(q_len, heads_in_launch, batch, sms) ? kTileM : 2 * kTileM;
+  return static_cast<long long>((q_len + rows - 1) / rows) * heads_in_launch * batch;
+}
+
 template <int HD>
 static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const AttnFwdParams& p, int heads_in_launch, int batch, int dev,
@@ -638,7 +656,9 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
   }
   AttnFwdParams q = p;
   q.heads_in_launch = heads_in_launch;
-  const long long items = static_cast<long long>(p.n_q_tiles) * heads_in_launch * batch;
+  q.single_tiles = single_tile_items(p.q_len, heads_in_launch, batch, sms) ? 1 : 0;
+  q.n_q_tiles = (p.q_len + (q.single_tiles ? kTileM : 2 * kTileM) - 1) / (q.single_tiles ? kTileM : 2 * kTileM);
+  const long long items = static_cast<long long>(q.n_q_tiles) * heads_in_launch * batch;
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   q.n_items = static_cast<int>(items);

@@ -20,7 +20,9 @@ struct AttnFwdParams {
   int kv_valid;          // keys >= kv_valid masked (already clamped to [1, kv_len])
   const int* kv_valid_dev;  // optional per-batch override (device)
   int causal;
-  int n_q_tiles;         // query tiles per head: pairs (attn_fwd_rows_per_cta()) or, wide, 128-row tiles
+  int n_q_tiles;         // query tiles per head: pairs or single 128-row tiles (head dims 64 / 128,
+                         // chosen by launch_attn_fwd), 128-row tiles (wide)
+  int single_tiles;      // set by launch_attn_fwd (head dims 64 / 128): items are single 128-row tiles
   int head_offset;       // first query head handled by this launch
   int heads_in_launch;   // set by launch_attn_fwd: query heads of this launch
   int n_items;           // set by launch_attn_fwd: n_q_tiles * heads_in_launch * batch
@@ -84,7 +86,10 @@ cudaError_t launch_attn_wide(const CUtensorMap& tq, const CUtensorMap& tk, const
                              const AttnFwdParams& p, int heads_in_launch, int batch, int dev,
                              cudaStream_t stream);
 
-int attn_fwd_rows_per_cta();  // query rows one attention CTA covers (head dims 64 / 128)
+int attn_fwd_rows_per_cta();  // query rows of a paired work item (head dims 64 / 128)
+// Work items launch_attn_fwd deals for head dims 64 / 128 (pairs of query
+// tiles, or single tiles when pairs would leave more than half of `sms` idle).
+long long attn_fwd_work_items(int q_len, int heads_in_launch, int batch, int sms);
 
 cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
 

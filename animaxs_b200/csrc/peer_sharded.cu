@@ -211,8 +211,8 @@ extern "C" int animaxs_attn_forward_head_sharded_peer(animaxs_attn_ctx* ctx, ani
                         static_cast<long long>(g->out_bytes));
   const int hr = d->heads / world;
   const int h0 = rank * hr;
-  const unsigned int items = static_cast<unsigned int>(
-      ((d->q_len + ax::attn_fwd_rows_per_cta() - 1) / ax::attn_fwd_rows_per_cta()) * hr * d->batch);
+  const unsigned int items =
+      static_cast<unsigned int>(ax::attn_fwd_work_items(d->q_len, hr, d->batch, ctx->num_sms));
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   DeviceGuard guard(ctx->device);
 
