@@ -9,15 +9,20 @@
 //   out[p+D/2] = sin*a +   cos*b        (a = x[p]*inv*w[p], b = x[p+D/2]*inv*w[p+D/2])
 // with the [token][D/2][2][2] table blocks [cos, -sin, sin, cos].
 //
-// HBM-bound (4*D bytes of traffic per row).  8 lanes work on one row: lane l
-// takes E = D/16 elements [E*l, E*l+E) and [D/2+E*l, D/2+E*l+E), i.e. both
-// members of rotation pairs E*l..E*l+E-1, so the rotation needs no data
-// exchange and only the sum of squares is reduced (3 shuffles).  One CTA per
-// (token, batch): its rows (the token's q heads, then its k heads) are dealt to
-// row slots of 8 lanes, four rows per slot, and every thread issues all of its
+// 4*D bytes of HBM traffic per row.  8 lanes work on one row: lane l takes
+// E = D/16 elements [E*l, E*l+E) and [D/2+E*l, D/2+E*l+E), i.e. both members
+// of rotation pairs E*l..E*l+E-1, so the rotation needs no data exchange and
+// only the sum of squares is reduced (3 shuffles).  One CTA per (token,
+// batch): its rows (the token's q heads, then its k heads) are dealt to row
+// slots of 8 lanes, four rows per slot, and every thread issues all of its
 // loads before any math so that enough bytes are in flight to cover HBM
-// latency (measured 4.9 TB/s on the fused DiT paths).  A lane's E rotation
-// blocks are loaded once per token and reused by every head.
+// latency.  The kernel is bound by L1 requests and issue slots rather than
+// DRAM, so it keeps those down: a lane's E rotation blocks are loaded once per
+// token, a quarter by each of the warp's 4 row slots and the rest passed by
+// shuffle; the two jobs' weights are loaded once per thread; the weight and
+// rotation products run as packed f32x2 instructions (per-element IEEE
+// results as the scalar forms, with the same fused multiply-add contraction).
+// Measured 4.8 TB/s for the fused DiT self-attention prologue.
 #include "kernels.h"
 #include "sm100_ptx.cuh"
 
@@ -55,7 +60,8 @@ __device__ __forceinline__ void store_chunk(__half* p, const Chunk<E>& c) {
 
 template <int HD>
 __device__ __forceinline__ void norm_row(const Chunk<HD / 16> ra, const Chunk<HD / 16> rb, __half* dst,
-                                         const __half* weight, float eps, bool rope,
+                                         bool has_w, const Chunk<HD / 16>& wa, const Chunk<HD / 16>& wb,
+                                         float eps, bool rope,
                                          const float (&c)[HD / 16], const float (&ns)[HD / 16],
                                          const float (&sn)[HD / 16], int l8, unsigned mask) {
   constexpr int E = HD / 16;
@@ -77,17 +83,19 @@ __device__ __forceinline__ void norm_row(const Chunk<HD / 16> ra, const Chunk<HD
   ss += __shfl_xor_sync(mask, ss, 2);
   ss += __shfl_xor_sync(mask, ss, 1);
   const float inv = rsqrtf(ss * (1.0f / HD) + eps);
-  if (weight != nullptr) {
-    const Chunk<E> wa = load_chunk<E>(weight + l8 * E);
-    const Chunk<E> wb = load_chunk<E>(weight + H2 + l8 * E);
+  if (has_w) {
+    const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
     for (int i = 0; i < E / 2; ++i) {
       const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&wa.w[i]));
       const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&wb.w[i]));
-      a[2 * i] *= inv * fa.x;
-      a[2 * i + 1] *= inv * fa.y;
-      b[2 * i] *= inv * fb.x;
-      b[2 * i + 1] *= inv * fb.y;
+      // a *= inv * w, two elements per instruction
+      const float2 xa = mul2(make_float2(a[2 * i], a[2 * i + 1]), mul2(inv2, fa));
+      const float2 xb = mul2(make_float2(b[2 * i], b[2 * i + 1]), mul2(inv2, fb));
+      a[2 * i] = xa.x;
+      a[2 * i + 1] = xa.y;
+      b[2 * i] = xb.x;
+      b[2 * i + 1] = xb.y;
     }
   } else {
 #pragma unroll
@@ -101,8 +109,12 @@ __device__ __forceinline__ void norm_row(const Chunk<HD / 16> ra, const Chunk<HD
 #pragma unroll
     for (int i = 0; i < E / 2; ++i) {
       const int e = 2 * i, f = 2 * i + 1;
-      __half2 x = __floats2half2_rn(c[e] * a[e] + ns[e] * b[e], c[f] * a[f] + ns[f] * b[f]);
-      __half2 y = __floats2half2_rn(sn[e] * a[e] + c[e] * b[e], sn[f] * a[f] + c[f] * b[f]);
+      // x = fma(cos, a, -sin * b), y = fma(sin, a, cos * b)
+      const float2 A = make_float2(a[e], a[f]), B = make_float2(b[e], b[f]), C = make_float2(c[e], c[f]);
+      const float2 X = fma2(C, A, mul2(make_float2(ns[e], ns[f]), B));
+      const float2 Y = fma2(make_float2(sn[e], sn[f]), A, mul2(C, B));
+      __half2 x = __floats2half2_rn(X.x, X.y);
+      __half2 y = __floats2half2_rn(Y.x, Y.y);
       oa.w[i] = *reinterpret_cast<uint32_t*>(&x);
       ob.w[i] = *reinterpret_cast<uint32_t*>(&y);
     }
@@ -131,15 +143,38 @@ __global__ void __launch_bounds__(kMaxNormThreads) qk_norm_kernel(const NormPara
   const bool rope = p.rope != nullptr;
   float c[E], ns[E], sn[E];
   if (rope) {
+    // The 4 row slots of a warp need the same blocks: slot s loads blocks
+    // [E/4 s, E/4 (s+1)) of its lane's E and the others come by shuffle.
     const float4* tab = reinterpret_cast<const float4*>(p.rope) + static_cast<long long>(tok) * H2 + l8 * E;
+    constexpr int Q = E / 4;
+    const int s4 = (threadIdx.x >> 3) & 3;
+    float4 mine[Q];
 #pragma unroll
-    for (int i = 0; i < E; ++i) { const float4 blk = __ldg(tab + i); c[i] = blk.x; ns[i] = blk.y; sn[i] = blk.z; }
+    for (int i = 0; i < Q; ++i) mine[i] = __ldg(tab + s4 * Q + i);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const int src = (threadIdx.x & 7) + 8 * (i / Q);
+      c[i] = __shfl_sync(0xffffffffu, mine[i % Q].x, src);
+      ns[i] = __shfl_sync(0xffffffffu, mine[i % Q].y, src);
+      sn[i] = __shfl_sync(0xffffffffu, mine[i % Q].z, src);
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < E; ++i) c[i] = ns[i] = sn[i] = 0.f;
   }
   const NormJob& J0 = p.job[0];
   const NormJob& J1 = p.job[1];
+  Chunk<E> wa0{}, wb0{}, wa1{}, wb1{};
+  const bool hw0 = J0.weight != nullptr;
+  const bool hw1 = p.njobs > 1 && J1.weight != nullptr;
+  if (hw0) {
+    wa0 = load_chunk<E>(J0.weight + l8 * E);
+    wb0 = load_chunk<E>(J0.weight + H2 + l8 * E);
+  }
+  if (hw1) {
+    wa1 = load_chunk<E>(J1.weight + l8 * E);
+    wb1 = load_chunk<E>(J1.weight + H2 + l8 * E);
+  }
   const int r0 = (tok < J0.tokens && bb < J0.batch) ? J0.heads : 0;
   const int r1 = (p.njobs > 1 && tok < J1.tokens && bb < J1.batch) ? J1.heads : 0;
   const int rows = r0 + r1;
@@ -147,25 +182,30 @@ __global__ void __launch_bounds__(kMaxNormThreads) qk_norm_kernel(const NormPara
   for (int base = 0; base < rows; base += kSlots * kRowUnroll) {
     Chunk<E> ra[kRowUnroll], rb[kRowUnroll];
     __half* dst[kRowUnroll];
-    const __half* w[kRowUnroll];
+    bool sec[kRowUnroll];
 #pragma unroll
     for (int u = 0; u < kRowUnroll; ++u) {
       const int r = base + slot + kSlots * u;
-      dst[u] = nullptr; w[u] = nullptr;
+      dst[u] = nullptr; sec[u] = false;
       if (r < rows) {
         const bool second = r >= r0;
         const NormJob& J = second ? J1 : J0;
         const int head = second ? r - r0 : r;
         const __half* src = J.in + bb * J.in_batch + static_cast<long long>(tok) * J.in_tok + static_cast<long long>(head) * J.in_head;
         dst[u] = J.out + bb * J.out_batch + static_cast<long long>(tok) * J.out_tok + static_cast<long long>(head) * J.out_head;
-        w[u] = J.weight;
+        sec[u] = second;
         ra[u] = load_chunk<E>(src + l8 * E);
         rb[u] = load_chunk<E>(src + H2 + l8 * E);
       }
     }
 #pragma unroll
     for (int u = 0; u < kRowUnroll; ++u)
-      if (dst[u] != nullptr) norm_row<HD>(ra[u], rb[u], dst[u], w[u], p.eps, rope, c, ns, sn, l8, mask);
+      if (dst[u] != nullptr) {
+        if (sec[u])
+          norm_row<HD>(ra[u], rb[u], dst[u], hw1, wa1, wb1, p.eps, rope, c, ns, sn, l8, mask);
+        else
+          norm_row<HD>(ra[u], rb[u], dst[u], hw0, wa0, wb0, p.eps, rope, c, ns, sn, l8, mask);
+      }
   }
 }
 
