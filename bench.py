@@ -335,12 +335,21 @@ def _packed_views(buf):
 
 def run_e2e(torch, ex, device, stream, rope, args, world):
     """Same metric through the fused C-ABI call with pinned host inputs/outputs.
-    Per block: one H2D copy of the block's packed q,k,v (self) + q,k,v (cross),
-    two fused attention calls, one D2H copy of both outputs; copies and compute
-    overlap across three streams."""
+    Per call: one H2D copy of the call's packed q,k,v (self) + q (cross), two
+    fused attention calls, one D2H copy of both outputs; copies and compute
+    overlap across three streams.  The cross-attention K/V of a block do not
+    change across the 8 Euler steps (the adapter context is fixed per prompt),
+    so, as the reference's DiT block executor does with its cross-K/V cache
+    (DiTBlockExecutor.swift:19-43, reuse at :1110-1161), each image uploads a
+    block's K/V once, at its first step, into a CrossKVCache (K normalised
+    there) and the cross calls normalise only q.  Every byte an image needs
+    crosses PCIe inside its own timed region."""
+    from animaxs_b200 import CrossKVCache
     nblk = 4
     g = torch.Generator().manual_seed(99)
     n_in = sum(int(torch.Size(shape).numel()) for _, shape in E2E_INPUTS)
+    n_ctx = sum(int(torch.Size(shape).numel()) for name, shape in E2E_INPUTS if name in ("ck", "cv"))
+    n_pre = n_in - n_ctx  # sq, sk, sv, cq: every call
     host = [torch.randn(n_in, generator=g).half().pin_memory() for _ in range(nblk)]
     n_out = 2 * S_SELF * HEADS * HD
     outs_h = [torch.empty(n_out, dtype=torch.float16).pin_memory() for _ in range(2)]
@@ -349,10 +358,11 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
     dev_out_buf = [torch.empty(n_out, dtype=torch.float16, device=device) for _ in range(2)]
     dev_out = [[b[:n_out // 2].view(1, S_SELF, HEADS, HD), b[n_out // 2:].view(1, S_SELF, HEADS, HD)]
                for b in dev_out_buf]
+    cache = CrossKVCache(ex, blocks=BLOCKS, batch=1, tokens=S_CTX, kv_heads=HEADS, head_dim=HD)
     s_in = torch.cuda.Stream(device)
     s_out = torch.cuda.Stream(device)
-    h2d = n_in * 2
-    d2h = n_out * 2
+    h2d = (n_pre * CALLS_PER_IMAGE + n_ctx * BLOCKS) * 2
+    d2h = n_out * 2 * CALLS_PER_IMAGE
 
     def one_image():
         in_ready = [None, None]
@@ -361,11 +371,14 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
         first = [True, True]
         for i in range(CALLS_PER_IMAGE):
             slot = i & 1
+            blk = i % BLOCKS
+            ctx_upload = i < BLOCKS  # the block's first Euler step
             src = host[i % nblk]
+            n = n_in if ctx_upload else n_pre
             with torch.cuda.stream(s_in):
                 if not first[slot]:
                     s_in.wait_event(comp_done[slot])
-                dev_buf[slot].copy_(src, non_blocking=True)
+                dev_buf[slot][:n].copy_(src[:n], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(s_in)
                 in_ready[slot] = ev
@@ -375,8 +388,10 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
             d = dev_in[slot]
             ex.attention(d["sq"], d["sk"], d["sv"], out=dev_out[slot][0], qk_norm="rms_rope",
                          rope_table=rope, stream=stream)
-            ex.attention(d["cq"], d["ck"], d["cv"], out=dev_out[slot][1], qk_norm="rms",
-                         stream=stream)
+            if ctx_upload:
+                cache.fill(blk, d["ck"], d["cv"], stream=stream)
+            ex.attention(d["cq"], cache.k(blk), cache.v(blk), out=dev_out[slot][1], qk_norm="rms",
+                         qk_norm_targets="q", stream=stream)
             comp_done[slot].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(comp_done[slot])
@@ -397,9 +412,11 @@ def run_e2e(torch, ex, device, stream, rope, args, world):
         t = torch.tensor([el], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         el = float(t.item())
+    cache.close()
     return {"value": steps * world / el, "unit": "img/s", "images_per_call": 1,
-            "h2d_bytes_per_step": h2d * CALLS_PER_IMAGE, "d2h_bytes_per_step": d2h * CALLS_PER_IMAGE,
-            "steps": steps, "path": "AttentionExecutor.attention -> animaxs_attn_forward (fused rms/rope)"}
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "path": "AttentionExecutor.attention -> animaxs_attn_forward (fused rms/rope); "
+                                    "cross K/V uploaded once per block and image into a CrossKVCache"}
 
 
 def _graph_us(torch, stream, calls, reps=3):
