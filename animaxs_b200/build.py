@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libanimaxs_attn.so")
 CALL_BENCH = os.path.join(BUILD, "call_bench")
-SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "attn_wide_sm100.cu", "qk_norm.cu", "sharded.cu",
+SOURCES = ["attn_api.cu", "attn_fwd_sm100.cu", "attn_s3_sm100.cu", "attn_wide_sm100.cu", "qk_norm.cu", "sharded.cu",
            "noalloc.cu", "proj_api.cu", "proj_sm100.cu", "dequant_sm100.cu",
            "peer_sync.cu", "peer_sharded.cu", "cross_kv_cache.cu", "weight_streamer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

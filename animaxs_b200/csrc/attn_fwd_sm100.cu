@@ -94,9 +94,6 @@ constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;  // O_A at kColO, O_B at kColO + HD
-constexpr uint32_t kIdescQK = idesc_f16_f32(128, 128, false);  // B = K tile, K-major
-template <int HD>
-constexpr uint32_t kIdescPV = idesc_f16_f32(128, HD, true);     // B = V tile, MN-major, N = HD
 // Register split (setmaxnreg): the kernel launches 3 warpgroups at the
 // compiler's per-thread count N (ptxas: 168); the two softmax warpgroups raise
 // theirs to AX_SOFTMAX_REGS and the MMA/TMA warpgroup lowers its to
@@ -105,49 +102,6 @@ constexpr uint32_t kIdescPV = idesc_f16_f32(128, HD, true);     // B = V tile, M
 // ptxas report before it links the library.
 #define AX_SOFTMAX_REGS 208
 #define AX_OTHER_REGS 88
-
-// Descriptors advance by constant offsets of their start-address field
-// (bits 0-13, address >> 4; every operand lies below 256 KiB of shared memory,
-// so the field never carries).  The loops are unrolled and run on the whole MMA
-// warp (one elected lane issues): the issue rate sits on the critical path.
-template <int HD>
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint32_t k_tile) {
-  const uint64_t a0 = kmajor_desc(q_tile, 0), b0 = kmajor_desc(k_tile, 0);
-#pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
-    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4);
-    umma_f16_ss_warp(d_tmem, a0 + off, b0 + off, kIdescQK, kk > 0 ? 1u : 0u);
-  }
-}
-// Half `hf` of O (+)= P V: k-steps 4*hf .. 4*hf+3 (keys [64*hf, 64*hf+64)).
-// kFp32P: P is held as P_hi (columns [0, 64) of the S tile) plus P_lo
-// (columns [64, 128)) and both are multiplied into the same accumulator.
-template <int HD, bool kFp32P>
-__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
-                                              int hf, bool accumulate) {
-  const uint64_t b0 = vmajor_desc(v_tile, 0);
-#pragma unroll
-  for (int k4 = 0; k4 < 4; ++k4) {
-    const int kk = hf * 4 + k4;
-    umma_f16_ts_warp(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV<HD>,
-                (accumulate || kk > 0) ? 1u : 0u);
-  }
-  if constexpr (kFp32P) {
-#pragma unroll
-    for (int k4 = 0; k4 < 4; ++k4) {
-      const int kk = hf * 4 + k4;
-      umma_f16_ts_warp(d_tmem, p_tmem + 64 + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4),
-                       kIdescPV<HD>, 1u);
-    }
-  }
-}
-
-__device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, int causal) {
-  if (tile_q0 >= q_len) return 0;
-  int e = valid;
-  if (causal) e = min(e, tile_q0 + kTileM);
-  return (e + kTileN - 1) / kTileN;
-}
 
 // kProbe: also record the scores' numerical health (animaxs_attn_set_score_probe);
 // kFp32P: the FP32_SCORES_AND_SOFTMAX numerics (exp2 on the SFU only, P x V
@@ -616,11 +570,11 @@ int attn_fwd_rows_per_cta() { return 2 * kTileM; }
 
 // Work items of a launch.  An item is normally a pair of 128-row query tiles
 // sharing one K/V stream; when the pairs would leave more than half of the SMs
-// idle, items are single tiles (the second softmax warpgroup then idles):
-// twice the CTAs, each ~30 % slower per key tile (its softmax runs with one
-// warp per sub-partition and nothing else to overlap), so the launch finishes
-// sooner.  Every row's arithmetic is the same in both forms, so the output
-// is bit-identical.
+// idle, items are single tiles: twice the CTAs, so the launch finishes sooner.
+// At head dim 128 such launches run attn_s3_sm100.cu (below); the single-tile
+// items of this kernel (head dim 64, the score probe, fp32 numerics, peer
+// stores) leave the second softmax warpgroup idle.  Every row's arithmetic is
+// the same in all forms, so the output is bit-identical.
 static bool single_tile_items(int q_len, int heads_in_launch, int batch, int sms) {
   const long long pairs = (q_len + 2 * kTileM - 1) / (2 * kTileM);
   return 2 * pairs * heads_in_launch * batch <= sms;
@@ -654,9 +608,18 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
     if (e != cudaSuccess) return e;
     sm_count[dev & 63].store(sms, std::memory_order_relaxed);
   }
+  const bool single = single_tile_items(p.q_len, heads_in_launch, batch, sms);
+  // Single-tile launches at head dim 128 go to attn_s3_sm100.cu, whose one
+  // query tile per CTA has three score buffers, so its softmax never waits for
+  // the tensor core (config 1: 24.4 -> 20.6 us, a Qwen layer 15.0 -> 13.8 us;
+  // same bits).  Paired launches stay here: with one softmax warp per SM
+  // sub-partition the other kernel cannot hide its own latencies the way two
+  // warpgroups hide each other's (batch-8 DiT self-attention 1035 vs 1104 us).
+  if (single && HD == 128 && p.probe == nullptr && !p.fp32_p && p.n_peers == 0)
+    return launch_attn_s3(tq, tk, tv, p, heads_in_launch, batch, dev, sms, stream);
   AttnFwdParams q = p;
   q.heads_in_launch = heads_in_launch;
-  q.single_tiles = single_tile_items(p.q_len, heads_in_launch, batch, sms) ? 1 : 0;
+  q.single_tiles = single ? 1 : 0;
   q.n_q_tiles = (p.q_len + (q.single_tiles ? kTileM : 2 * kTileM) - 1) / (q.single_tiles ? kTileM : 2 * kTileM);
   const long long items = static_cast<long long>(q.n_q_tiles) * heads_in_launch * batch;
   if (items <= 0) return cudaSuccess;

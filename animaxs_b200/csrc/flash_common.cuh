@@ -4,6 +4,7 @@
 // SW128 panels, the lazy-rescale threshold and the FMA-pipe exp2.
 #pragma once
 
+#include "kernels.h"
 #include "sm100_ptx.cuh"
 
 namespace ax {
@@ -49,6 +50,55 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int kk) {
 // rows (1024 B apart); the two 64-wide head_dim panels are kPanelBytes apart.
 __device__ __forceinline__ uint64_t vmajor_desc(uint32_t tile, int kk) {
   return sw128_desc(tile + kk * 2048, kPanelBytes, 1024);
+}
+
+
+// ---- MMA issue for 128-row tiles (attn_fwd_sm100.cu, attn_s3_sm100.cu) ----
+constexpr uint32_t kIdescQKTile = idesc_f16_f32(128, 128, false);  // B = K tile, K-major
+template <int HD>
+constexpr uint32_t kIdescPVTile = idesc_f16_f32(128, HD, true);     // B = V tile, MN-major, N = HD
+
+// Descriptors advance by constant offsets of their start-address field
+// (bits 0-13, address >> 4; every operand lies below 256 KiB of shared memory,
+// so the field never carries).  The loops are unrolled and run on the whole MMA
+// warp (one elected lane issues): the issue rate sits on the critical path.
+template <int HD>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_tile, uint32_t k_tile) {
+  const uint64_t a0 = kmajor_desc(q_tile, 0), b0 = kmajor_desc(k_tile, 0);
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4);
+    umma_f16_ss_warp(d_tmem, a0 + off, b0 + off, kIdescQKTile, kk > 0 ? 1u : 0u);
+  }
+}
+// Half `hf` of O (+)= P V: k-steps 4*hf .. 4*hf+3 (keys [64*hf, 64*hf+64)).
+// kFp32P: P is held as P_hi (columns [0, 64) of the S tile) plus P_lo
+// (columns [64, 128)) and both are multiplied into the same accumulator.
+template <int HD, bool kFp32P>
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_tile,
+                                              int hf, bool accumulate) {
+  const uint64_t b0 = vmajor_desc(v_tile, 0);
+#pragma unroll
+  for (int k4 = 0; k4 < 4; ++k4) {
+    const int kk = hf * 4 + k4;
+    umma_f16_ts_warp(d_tmem, p_tmem + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPVTile<HD>,
+                (accumulate || kk > 0) ? 1u : 0u);
+  }
+  if constexpr (kFp32P) {
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+      const int kk = hf * 4 + k4;
+      umma_f16_ts_warp(d_tmem, p_tmem + 64 + kk * 8, b0 + static_cast<uint64_t>((kk * 2048) >> 4),
+                       kIdescPVTile<HD>, 1u);
+    }
+  }
+}
+
+__device__ __forceinline__ int kv_tiles_for(int tile_q0, int q_len, int valid, int causal) {
+  if (tile_q0 >= q_len) return 0;
+  int e = valid;
+  if (causal) e = min(e, tile_q0 + kTileM);
+  return (e + kTileN - 1) / kTileN;
 }
 
 }  // namespace ax

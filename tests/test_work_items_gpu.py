@@ -1,7 +1,9 @@
-"""GPU: work items of the flash kernel.  A launch whose query-tile pairs would
+"""GPU: work items of the flash kernels.  A launch whose query-tile pairs would
 leave more than half of the SMs idle deals single 128-row tiles instead (twice
-the CTAs); every row's arithmetic is the same either way, so the output must
-be BIT-IDENTICAL to the paired form.  The same inputs are run alone (single
+the CTAs); at head_dim 128 those launches run attn_s3_sm100.cu (one tile per
+CTA, three score buffers), at head_dim 64 the paired kernel's chain A alone.
+Every row's arithmetic is the same in all of them, so the output must be
+BIT-IDENTICAL to the paired form.  The same inputs are run alone (single
 tiles: few pairs) and as image 0 of a batch large enough to be dealt in pairs,
 and compared; the single-tile launch is also checked against the oracle."""
 import numpy as np
