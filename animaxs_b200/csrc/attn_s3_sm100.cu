@@ -5,9 +5,11 @@
 // (AttentionExecutor.swift:122-302; AnimaKernels.metal:2193-2318): an online
 // softmax over 128-key tiles with fp32 statistics, the lazy O rescale (only
 // when a row's max grows by more than 2^8), exp2 on the MUFU and FMA pipes in
-// the same column pairs, P published in two halves and multiplied in two
-// halves.  Each row goes through exactly the instructions of a chain of
-// attn_fwd_sm100.cu, so the two kernels produce the same bits.
+// the same column pairs, P written as fp16 over the consumed scores and
+// multiplied in the same two halves.  Each row goes through exactly the
+// arithmetic of a chain of attn_fwd_sm100.cu, so the two kernels produce the
+// same bits (P is published once per tile here: the softmax does not wait for
+// the tensor core, so half-tile publication would gain nothing).
 //
 // What differs is the pipeline.  attn_fwd_sm100.cu runs two query tiles per
 // CTA with one score buffer each, so every tile's chain is softmax(j) ->
@@ -28,6 +30,9 @@
 //        publishes the count in shared memory, so that a softmax thread that
 //        must rescale O (rare) can wait for exactly the PVs it needs
 //   7    idle
+// Used for the launches that deal single tiles; paired launches run
+// attn_fwd_sm100.cu, whose two softmax warpgroups per SM hide each other's
+// latencies (one warp per SM sub-partition cannot).
 // Every wait is bounded (ANIMAXS_WAIT_TIMEOUT_NS); a timeout raises the CTA's
 // abort flag and the device status bit, and the CTA drains and exits.
 #include <atomic>
