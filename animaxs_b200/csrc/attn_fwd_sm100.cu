@@ -609,13 +609,13 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
     sm_count[dev & 63].store(sms, std::memory_order_relaxed);
   }
   const bool single = single_tile_items(p.q_len, heads_in_launch, batch, sms);
-  // Single-tile launches at head dim 128 go to attn_s3_sm100.cu, whose one
+  // Single-tile launches go to attn_s3_sm100.cu, whose one
   // query tile per CTA has three score buffers, so its softmax never waits for
   // the tensor core (config 1: 24.4 -> 20.6 us, a Qwen layer 15.0 -> 13.8 us;
   // same bits).  Paired launches stay here: with one softmax warp per SM
   // sub-partition the other kernel cannot hide its own latencies the way two
   // warpgroups hide each other's (batch-8 DiT self-attention 1035 vs 1104 us).
-  if (single && HD == 128 && p.probe == nullptr && !p.fp32_p && p.n_peers == 0)
+  if (single && p.probe == nullptr && !p.fp32_p && p.n_peers == 0)
     return launch_attn_s3(tq, tk, tv, p, heads_in_launch, batch, dev, sms, stream);
   AttnFwdParams q = p;
   q.heads_in_launch = heads_in_launch;

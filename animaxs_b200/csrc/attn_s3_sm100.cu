@@ -1,4 +1,4 @@
-// attn_s3_sm100.cu -- flash attention for head_dim 128 on B200 (sm_100a): one
+// attn_s3_sm100.cu -- flash attention for head_dim 64 / 128 on B200 (sm_100a): one
 // query tile per work item, three score buffers in TMEM.
 //
 // The same operator and the same per-row arithmetic as attn_fwd_sm100.cu
@@ -47,9 +47,9 @@ namespace {
 constexpr int kS3KStages = 3;
 constexpr int kS3VStages = 2;
 constexpr int kS3SBufs = 3;
-constexpr int kS3HD = 128;
+template <int HD>
 struct S3Smem {
-  static constexpr uint32_t kTile = kTileM * kS3HD * 2;  // 32 KiB
+  static constexpr uint32_t kTile = kTileM * HD * 2;  // 32 KiB (HD 128) / 16 KiB (HD 64)
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kK = kQ + kTile;
   static constexpr uint32_t kV = kK + kS3KStages * kTile;
@@ -59,7 +59,7 @@ struct S3Smem {
   static constexpr uint32_t kStage = kBar + 1024;
   static constexpr uint32_t kBytes = kStage + 4 * 4096 + 1024;  // + alignment slack
 };
-static_assert(S3Smem::kBytes <= 227 * 1024, "shared memory exceeds the 227 KiB opt-in");
+static_assert(S3Smem<128>::kBytes <= 227 * 1024, "shared memory exceeds the 227 KiB opt-in");
 constexpr int kS3Threads = 256;
 
 // The K ring has one stage per score buffer: K tile t lives in stage t % 3
@@ -96,16 +96,16 @@ __device__ __forceinline__ void st_release_cta(volatile uint32_t* p, uint32_t v)
   asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(const_cast<uint32_t*>(p))), "r"(v) : "memory");
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kS3Threads, 1)
     attn_s3_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                          const AttnFwdParams p) {
-  constexpr int HD = kS3HD;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  using L = S3Smem;
+  using L = S3Smem<HD>;
   constexpr uint32_t kTileBytes = L::kTile;
   const uint32_t sQ = base + L::kQ, sK = base + L::kK, sV = base + L::kV;
   const uint32_t bar0 = base + L::kBar;
@@ -468,16 +468,19 @@ __global__ void __launch_bounds__(kS3Threads, 1)
 
 }  // namespace
 
-// One query tile per work item (n_q_tiles = ceil(q_len / 128)); head dim 128,
-// no score probe, legacy numerics, no peer stores (launch_attn_fwd checks).
-cudaError_t launch_attn_s3(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                           const AttnFwdParams& p, int heads_in_launch, int batch, int dev, int sms,
-                           cudaStream_t stream) {
+// One query tile per work item (n_q_tiles = ceil(q_len / 128)); head dim 64
+// or 128, no score probe, legacy numerics, no peer stores (launch_attn_fwd
+// checks).
+template <int HD>
+static cudaError_t launch_s3_hd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                                const AttnFwdParams& p, int heads_in_launch, int batch, int dev, int sms,
+                                cudaStream_t stream) {
   static std::atomic<uint64_t> configured{0};
   cudaError_t e;
   const uint64_t bit = 1ull << (dev & 63);
   if ((configured.load(std::memory_order_acquire) & bit) == 0) {
-    e = cudaFuncSetAttribute(attn_s3_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S3Smem::kBytes);
+    e = cudaFuncSetAttribute(attn_s3_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             S3Smem<HD>::kBytes);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
@@ -490,13 +493,21 @@ cudaError_t launch_attn_s3(const CUtensorMap& tq, const CUtensorMap& tk, const C
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   q.n_items = static_cast<int>(items);
   const int grid = static_cast<int>(items < sms ? items : sms);
-  // Output view [batch][heads][q_len][128] for the tensor stores (box 64 x 32).
+  // Output view [batch][heads][q_len][HD] for the tensor stores (box 64 x 32).
   CUtensorMap to;
-  if (ax_make_tmap(nullptr, &to, p.o, kS3HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
+  if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
                    p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
     return cudaErrorInvalidValue;
-  attn_s3_sm100_kernel<<<grid, kS3Threads, S3Smem::kBytes, stream>>>(tq, tk, tv, to, q);
+  attn_s3_sm100_kernel<HD><<<grid, kS3Threads, S3Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attn_s3(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                           const AttnFwdParams& p, int heads_in_launch, int batch, int dev, int sms,
+                           cudaStream_t stream) {
+  if (p.head_dim == 64) return launch_s3_hd<64>(tq, tk, tv, p, heads_in_launch, batch, dev, sms, stream);
+  if (p.head_dim == 128) return launch_s3_hd<128>(tq, tk, tv, p, heads_in_launch, batch, dev, sms, stream);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace ax

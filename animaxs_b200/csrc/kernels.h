@@ -81,7 +81,7 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const 
                             const AttnFwdParams& p, int heads_in_launch, int batch,
                             cudaStream_t stream);
 
-// Head dim 128, one query tile per item with three score buffers in TMEM
+// Head dim 64 / 128, one query tile per item with three score buffers in TMEM
 // (attn_s3_sm100.cu; called by launch_attn_fwd).
 cudaError_t launch_attn_s3(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                            const AttnFwdParams& p, int heads_in_launch, int batch, int dev, int sms,

@@ -1,7 +1,6 @@
 """GPU: work items of the flash kernels.  A launch whose query-tile pairs would
 leave more than half of the SMs idle deals single 128-row tiles instead (twice
-the CTAs); at head_dim 128 those launches run attn_s3_sm100.cu (one tile per
-CTA, three score buffers), at head_dim 64 the paired kernel's chain A alone.
+the CTAs) and runs attn_s3_sm100.cu (one tile per CTA, three score buffers).
 Every row's arithmetic is the same in all of them, so the output must be
 BIT-IDENTICAL to the paired form.  The same inputs are run alone (single
 tiles: few pairs) and as image 0 of a batch large enough to be dealt in pairs,
