@@ -1063,6 +1063,20 @@ def profile_kernel(args):
         ex.synchronize()
         print("profile-kernel done", flush=True)
         return
+    if args.workload == "cfg1":
+        # warmup + steps configuration-1 calls (1024 tokens x 16 heads, batch 1: a
+        # single-tile launch, attn_s3_sm100_kernel; the inputs stay in L2 as in
+        # the configuration itself)
+        g = torch.Generator(device="cuda").manual_seed(5)
+        q, k, v = (torch.randn(1, 1024, HEADS, HD, generator=g, device="cuda").half() for _ in range(3))
+        out = torch.empty_like(q)
+        rope = torch.from_numpy(ax.DitRoPE.generate(1, 32, 32).reshape(1024, 64, 2, 2)).cuda()
+        for _ in range(args.warmup + args.steps):
+            ex.attention(q, k, v, out=out, qk_norm="rms_rope", rope_table=rope)
+        torch.cuda.synchronize()
+        ex.synchronize()
+        print("profile-kernel done", flush=True)
+        return
     g = torch.Generator(device="cuda").manual_seed(5)
     shape = (4, S_SELF, HEADS, HD)
     q, k, v = (torch.randn(*shape, generator=g, device="cuda").half() for _ in range(3))
@@ -1091,11 +1105,12 @@ def main():
                     help="config-5 gather across ranks: fused NVLink stores or NCCL all-gather")
     ap.add_argument("--weights", default="fp16", choices=["fp16", "w8", "w4"],
                     help="projection weight storage for --workload proj")
-    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae", "proj"],
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5", "vae", "proj", "cfg1"],
                     help="cfg4 (default): the 8-step DiT workload, batch-sharded; cfg5: the "
                          "16384-token self-attention, heads sharded + one NCCL all-gather; vae: "
                          "the VAE decoder's middle attention (one head of 384), images per rank; "
-                         "proj: the fused projections around DiT attention")
+                         "proj: the fused projections around DiT attention; cfg1 (with "
+                         "--profile-kernel only): configuration 1's calls")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only run the fused rms+rope3d self-attention (prologue + flash kernel) "
                          "on a batch-4 4096-token case (192 MiB of inputs, > L2), or with "
@@ -1111,6 +1126,8 @@ def main():
     if args.profile_kernel:
         profile_kernel(args)
         return
+    if args.workload == "cfg1":
+        ap.error("--workload cfg1 is a --profile-kernel case (configuration 1 is timed in the secondary block)")
     if world > 1:
         import datetime
 
