@@ -539,6 +539,7 @@ def secondary_configs(torch, ax, ex, device, args):
             "cpu_oracle_s": cpu_s, "cpu_oracle": cpu_note, "cpu_cores": os.cpu_count() or 1,
         }
         del dv, outs
+    out["rows_f"] = rows_f_figures(torch, ax, ex, device, stream, peak_sust, peak_burst)
     out["peak_kind"] = f"{peak_kind} bf16 dense"
     exe = os.path.join(ROOT, "animaxs_b200", "_build", "call_bench")
     try:
@@ -547,6 +548,124 @@ def secondary_configs(torch, ax, ex, device, args):
     except Exception as e:  # noqa: BLE001 -- reported in the line, not fatal
         out["c_abi"] = {"error": str(e)}
     return out
+
+
+def rows_f_figures(torch, ax, ex, device, stream, peak_sust, peak_burst):
+    """The kernels around the DiT attention call, each timed on its own with
+    a parity check against the oracle: the VAE's middle attention (1 head x 384
+    over 4096 positions, inputs cycled over 16 images > L2), the LLM adapter's
+    attention (512 tokens x 16 heads x 64, rms + RoPE), the fused q|k|v
+    projection of a batch-8 block ([32768, 2048] -> [32768, 6144], q/k RMSNorm +
+    3-D RoPE in the epilogue; parity on the first 256 rows) and the W4 weight
+    decode ([6144, 2048], bit-exact).  kernel_us: CUDA events around each
+    launch (animaxs_attn_kernel_timing); graph_us: whole calls replayed from a
+    CUDA graph."""
+    import numpy as np
+
+    from oracle import attn_oracle as ora  # the checker
+    from oracle import inputs
+    res = {}
+
+    def kernel_us(calls):
+        ex.set_kernel_timing(True)
+        with torch.cuda.stream(stream):
+            calls()
+        torch.cuda.synchronize()
+        ex.set_kernel_timing(False)
+        n_k, tot_ms, _ = ex.kernel_timing()
+        return tot_ms * 1e3 / n_k
+
+    def tflops(flops, us):
+        t = flops / (us * 1e-6) / 1e12
+        return {"tflops": t, "frac_sustained": t / peak_sust, "frac_burst": t / peak_burst}
+
+    # VAE middle attention: the oracle on the first 512 query rows of image 0.
+    case = inputs.vae_attention(seed=0)
+    g = torch.Generator(device=device).manual_seed(4321)
+    pool = [torch.from_numpy(np.concatenate([case.q, case.k, case.v], axis=0)).to(device)]
+    pool += [torch.randn(3, VAE_POS, 1, VAE_CH, generator=g, device=device).half() for _ in range(VAE_POOL - 1)]
+    vo = torch.empty(1, VAE_POS, 1, VAE_CH, dtype=torch.float16, device=device)
+
+    def vae_calls():
+        for x in pool:
+            ex.attention(x[0:1], x[1:2], x[2:3], out=vo, stream=torch.cuda.current_stream(device))
+        return len(pool)
+    g_us = _graph_us(torch, stream, vae_calls)
+    k_us = kernel_us(vae_calls)
+    ex.attention(pool[0][0:1], pool[0][1:2], pool[0][2:3], out=vo, stream=stream)
+    torch.cuda.synchronize()
+    ex.synchronize(stream)
+    rows = np.arange(512)
+    mx, mn = ora.parity(vo.float().cpu().numpy()[:, :512], case.oracle(rows=rows))
+    res["vae_hd384_4096"] = {"graph_us": g_us, "kernel_us": k_us, **tflops(VAE_FLOPS, k_us),
+                             "max_abs": mx, "mean_abs": mn, "parity_ok": bool(mx <= 2e-3 and mn <= 2e-4),
+                             "parity_rows": "512 of 4096 query rows"}
+
+    # LLM adapter attention, head dim 64 (the oracle on every row).
+    case = inputs.adapter_attention(seed=0)
+    aq, ak, av = (torch.from_numpy(x).to(device) for x in (case.q, case.k, case.v))
+    arope = torch.from_numpy(case.rope_table).to(device)
+    ao = torch.empty_like(aq)
+
+    def adapter_calls(reps=40):
+        for _ in range(reps):
+            ex.attention(aq, ak, av, out=ao, qk_norm="rms_rope", rope_table=arope,
+                         stream=torch.cuda.current_stream(device))
+        return reps
+    g_us = _graph_us(torch, stream, adapter_calls)
+    k_us = kernel_us(adapter_calls)
+    torch.cuda.synchronize()
+    ex.synchronize(stream)
+    mx, mn = ora.parity(ao.float().cpu().numpy(), case.oracle())
+    res["adapter_hd64_512x16"] = {"graph_us": g_us, "kernel_us": k_us, **tflops(case.flops(), k_us),
+                                  "max_abs": mx, "mean_abs": mn, "parity_ok": bool(mx <= 2e-3 and mn <= 2e-4)}
+
+    # Fused q|k|v projection of a batch-8 block.
+    pj = ax.ProjectionExecutor(ex)
+    gp = torch.Generator(device=device).manual_seed(2024)
+    m = BATCH * S_SELF
+    x = torch.randn(m, D_MODEL, generator=gp, device=device).half()
+    w = (torch.randn(3 * D_MODEL, D_MODEL, generator=gp, device=device) / D_MODEL ** 0.5).half()
+    qw = (1 + 0.1 * torch.randn(HD, generator=gp, device=device)).half()
+    kw = (1 + 0.1 * torch.randn(HD, generator=gp, device=device)).half()
+    tab = ora.dit_rope_table(1, 64, 64)
+    rope = torch.from_numpy(tab).to(device)
+    y = torch.empty(m, 3 * D_MODEL, dtype=torch.float16, device=device)
+
+    def proj_calls(reps=4):
+        for _ in range(reps):
+            pj.qkv(x, w, y, q_cols=D_MODEL, k_cols=D_MODEL, qk_norm="rms_rope", q_norm_weight=qw,
+                   k_norm_weight=kw, rope_table=rope, tokens=S_SELF, stream=torch.cuda.current_stream(device))
+        return reps
+    g_us = _graph_us(torch, stream, proj_calls)
+    k_us = kernel_us(proj_calls)
+    torch.cuda.synchronize()
+    want = ora.qkv_norm_projection(x[:256].cpu().numpy(), w.cpu().numpy(), q_cols=D_MODEL, k_cols=D_MODEL,
+                                   q_norm_weight=qw.cpu().numpy(), k_norm_weight=kw.cpu().numpy(),
+                                   rope_table=tab[:256], tokens=256)  # rows 0-255 = tokens 0-255 of image 0
+    want16 = ora.to_fp16_storage(want)
+    err = np.abs(y[:256].float().cpu().numpy() - want16)
+    bound_ok = bool((err <= 2e-3 + 2e-3 * np.abs(want16)).all()
+                    and err.mean() <= 2.0 ** -13 * float(np.abs(want16).mean()) + 1e-6)
+    res["proj_qkv_rms_rope3d_batch8"] = {"graph_us": g_us, "kernel_us": k_us,
+                                         **tflops(2.0 * m * 3 * D_MODEL * D_MODEL, k_us),
+                                         "max_abs": float(err.max()), "mean_abs": float(err.mean()),
+                                         "parity_ok": bound_ok,
+                                         "parity_rows": "first 256 rows; |d| <= 2e-3 + 2e-3 |oracle|, mean "
+                                                        "<= 2^-13 mean |oracle|"}
+    del x, y
+
+    # W4 decode: roofline on 6 weights cycled (> L2), bit-exact on one.
+    packed, scale, zero = inputs.quant_weight(4, 3 * D_MODEL, D_MODEL, 4)
+    qw4 = ax.QuantizedWeight(*(torch.from_numpy(a).to(device) for a in (packed, scale, zero)), 4, D_MODEL)
+    dec = pj.dequant(qw4, stream=stream)
+    torch.cuda.synchronize()
+    exact = bool(np.array_equal(dec.cpu().numpy().view(np.uint16),
+                                ora.dequant_to_half(packed, scale, zero, bits=4, k=D_MODEL).view(np.uint16)))
+    # (decode_roofline records its events on the stream its graph replays on)
+    res["dequant_w4_6144x2048"] = {**decode_roofline(pj, 4, device, torch.cuda.current_stream(device)),
+                                   "bit_exact": exact}
+    return res
 
 
 def cfg5_sharded(torch, dist, ex, rank, world, local_rank, steps=20, warmup=3):
