@@ -49,7 +49,7 @@ POOL_BLOCKS = 3                                   # distinct resident input sets
 # DRAM bytes (read + write) of one batch-8 self-attention flash launch: the ncu
 # capture in profiles/attn_fwd_sm100_selfattn4096_batch4.md measured 245.5 MB
 # for batch 4; traffic scales with the batch.
-TRAFFIC_PER_LAUNCH_MB = 491.0
+TRAFFIC_PER_LAUNCH_MB = 490.8
 
 METRIC = ("DiT attention throughput, 8-step 1024x1024 workload "
           "(28 blocks x 8 steps x [4096-tok self rms+rope3d + 4096x512 cross rms])")
