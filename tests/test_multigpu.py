@@ -244,7 +244,7 @@ def test_peer_fused_head_sharded_matches_single_gpu():
         assert out[rank] == [0.0] * 5, f"rank {rank}: max differences {out[rank]}"
 
 
-def _peer_absent_worker(rank, world, port, out):
+def _peer_absent_worker(rank, world, port, out, one_gpu=False):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
     import torch.distributed as dist
@@ -252,10 +252,11 @@ def _peer_absent_worker(rank, world, port, out):
     import animaxs_b200 as ax
     from animaxs_b200 import AttentionTimeoutError
     from animaxs_b200.sharded import PeerShardedAttention
-    torch.cuda.set_device(rank)
+    device = 0 if one_gpu else rank
+    torch.cuda.set_device(device)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world)
-    ex = ax.AttentionExecutor(rank)
+    ex = ax.AttentionExecutor(device)
     ps = PeerShardedAttention(ex, rank, world, (1, 512, 16, 128))
     if rank == 1:
         # A sentinel in rank 1's output: rank 0's call must not store into a
@@ -296,6 +297,23 @@ def test_peer_that_never_calls_times_out():
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_peer_absent_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    assert out[0] == "timeout" and out["after"]
+    assert out["untouched"], "rank 0 stored into rank 1's output after its ready handshake timed out"
+
+
+@pytest.mark.gpu
+@pytest.mark.timeout(180)
+def test_peer_that_never_calls_times_out_on_one_gpu():
+    """The same failure with both ranks as processes on one GPU (CUDA IPC
+    maps a buffer of the same device into the other process).  Rank 1 never
+    launches anything, so rank 0's bounded waits are the only kernels that
+    wait: the opening handshake gives up after 2 s, the attention kernel
+    stores nothing into rank 1's buffer and adds no arrival, the closing wait
+    gives up, synchronize reports the timeout and the context keeps working."""
+    import torch.multiprocessing as mp
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.spawn(_peer_absent_worker, args=(2, _free_port(), out, True), nprocs=2, join=True)
     assert out[0] == "timeout" and out["after"]
     assert out["untouched"], "rank 0 stored into rank 1's output after its ready handshake timed out"
 
