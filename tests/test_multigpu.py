@@ -138,7 +138,7 @@ def test_head_sharded_matches_single_gpu():
             assert err == 0.0, f"rank {rank} {layout}-major output differs by {err}"
 
 
-def _absent_peer_worker(rank, world, port, out):
+def _absent_peer_worker(rank, world, port, out, one_gpu=False):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["ANIMAXS_NCCL_TIMEOUT_S"] = "5"
     import torch
@@ -147,10 +147,11 @@ def _absent_peer_worker(rank, world, port, out):
     import animaxs_b200 as ax
     from animaxs_b200 import AttentionTimeoutError
     from animaxs_b200.sharded import HeadShardedAttention, share_unique_id
-    torch.cuda.set_device(rank)
+    device = 0 if one_gpu else rank
+    torch.cuda.set_device(device)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world)
-    ex = ax.AttentionExecutor(rank)
+    ex = ax.AttentionExecutor(device)
     uid = share_unique_id()
     if rank == 0:
         try:
@@ -172,6 +173,20 @@ def test_rank_that_never_joins_times_out():
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_absent_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    assert out[0] == "timeout"
+
+
+@pytest.mark.gpu
+@pytest.mark.timeout(180)
+def test_rank_that_never_joins_times_out_on_one_gpu():
+    """The communicator deadline with both ranks as processes on one GPU:
+    rank 1 never creates its communicator, so rank 0's non-blocking NCCL
+    initialisation waits in the bootstrap (no kernel runs) until the 5 s
+    deadline and reports the timeout."""
+    import torch.multiprocessing as mp
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.spawn(_absent_peer_worker, args=(2, _free_port(), out, True), nprocs=2, join=True)
     assert out[0] == "timeout"
 
 
