@@ -571,16 +571,19 @@ int attn_fwd_rows_per_cta() { return 2 * kTileM; }
 // Work items of a launch.  An item is normally a pair of 128-row query tiles
 // sharing one K/V stream; when the pairs would leave more than half of the SMs
 // idle, items are single tiles: twice the CTAs, so the launch finishes sooner.
-// At head dim 128 such launches run attn_s3_sm100.cu (below); the single-tile
-// items of this kernel (head dim 64, the score probe, fp32 numerics, peer
-// stores) leave the second softmax warpgroup idle.  Every row's arithmetic is
-// the same in all forms, so the output is bit-identical.
-static bool single_tile_items(int q_len, int heads_in_launch, int batch, int sms) {
-  const long long pairs = (q_len + 2 * kTileM - 1) / (2 * kTileM);
-  return 2 * pairs * heads_in_launch * batch <= sms;
+// Such launches run attn_s3_sm100.cu (below); the single-tile items of this
+// kernel (the score probe, fp32 numerics) leave the second softmax warpgroup
+// idle.  A launch whose output tiles also go to peer GPUs deals single tiles
+// as soon as the pairs alone would leave SMs idle: the pairs would all finish
+// at once and expose the whole gather, while single tiles take two waves and
+// the first wave's peer stores overlap the second wave.  Every row's
+// arithmetic is the same in all forms, so the output is bit-identical.
+static bool single_tile_items(int q_len, int heads_in_launch, int batch, int sms, bool peers) {
+  const long long pairs = (q_len + 2 * kTileM - 1) / (2 * kTileM) * static_cast<long long>(heads_in_launch) * batch;
+  return 2 * pairs <= sms || (peers && pairs < sms);
 }
-long long attn_fwd_work_items(int q_len, int heads_in_launch, int batch, int sms) {
-  const int rows = single_tile_items(q_len, heads_in_launch, batch, sms) ? kTileM : 2 * kTileM;
+long long attn_fwd_work_items(int q_len, int heads_in_launch, int batch, int sms, bool peers) {
+  const int rows = single_tile_items(q_len, heads_in_launch, batch, sms, peers) ? kTileM : 2 * kTileM;
   return static_cast<long long>((q_len + rows - 1) / rows) * heads_in_launch * batch;
 }
 
@@ -608,14 +611,14 @@ static cudaError_t launch_hd(const CUtensorMap& tq, const CUtensorMap& tk, const
     if (e != cudaSuccess) return e;
     sm_count[dev & 63].store(sms, std::memory_order_relaxed);
   }
-  const bool single = single_tile_items(p.q_len, heads_in_launch, batch, sms);
+  const bool single = single_tile_items(p.q_len, heads_in_launch, batch, sms, p.n_peers > 0);
   // Single-tile launches go to attn_s3_sm100.cu, whose one
   // query tile per CTA has three score buffers, so its softmax never waits for
   // the tensor core (config 1: 24.4 -> 20.6 us, a Qwen layer 15.0 -> 13.8 us;
   // same bits).  Paired launches stay here: with one softmax warp per SM
   // sub-partition the other kernel cannot hide its own latencies the way two
   // warpgroups hide each other's (batch-8 DiT self-attention 1035 vs 1104 us).
-  if (single && p.probe == nullptr && !p.fp32_p && p.n_peers == 0)
+  if (single && p.probe == nullptr && !p.fp32_p)
     return launch_attn_s3(tq, tk, tv, p, heads_in_launch, batch, dev, sms, stream);
   AttnFwdParams q = p;
   q.heads_in_launch = heads_in_launch;

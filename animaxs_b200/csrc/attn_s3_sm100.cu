@@ -32,7 +32,10 @@
 //   7    idle
 // Used for the launches that deal single tiles; paired launches run
 // attn_fwd_sm100.cu, whose two softmax warpgroups per SM hide each other's
-// latencies (one warp per SM sub-partition cannot).
+// latencies (one warp per SM sub-partition cannot).  In the fused
+// head-sharded gather (peer_sharded.cu) the epilogue also stores each output
+// tile into every peer's buffer and counts the CTA's items on the peers'
+// arrival words, as attn_fwd_sm100.cu does.
 // Every wait is bounded (ANIMAXS_WAIT_TIMEOUT_NS); a timeout raises the CTA's
 // abort flag and the device status bit, and the CTA drains and exits.
 #include <atomic>
@@ -96,7 +99,9 @@ __device__ __forceinline__ void st_release_cta(volatile uint32_t* p, uint32_t v)
   asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(const_cast<uint32_t*>(p))), "r"(v) : "memory");
 }
 
-template <int HD>
+// kPeers: the fused head-sharded gather's instantiation (peer stores and
+// arrivals); a separate instantiation, so that the others carry no trace of it.
+template <int HD, bool kPeers>
 __global__ void __launch_bounds__(kS3Threads, 1)
     attn_s3_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -138,6 +143,8 @@ __global__ void __launch_bounds__(kS3Threads, 1)
   };
   const int w0 = static_cast<int>(blockIdx.x);
   const int wstep = static_cast<int>(gridDim.x);
+  // Fused head-sharded gather: store into the peers only after a completed handshake.
+  const bool peers_go = kPeers && p.n_peers > 0 && (p.peer_go == nullptr || *p.peer_go == p.peer_go_value);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kS3NumBars; ++i)
@@ -448,6 +455,27 @@ __global__ void __launch_bounds__(kS3Threads, 1)
               tma_store_4d(&tm_o, wstage, 64 * rd, I.q0 + warp * 32, I.h - p.o_head_base, I.b);
               tma_store_commit();
             }
+            if (peers_go) {
+              // Fused head-sharded gather: the same 32 x 64 tile to the same
+              // place in every peer's output over NVLink, 8 lanes per row
+              // (128 contiguous bytes), 4 rows per step.  The stage is only
+              // read here; the next round rewrites it after the __syncwarp
+              // that follows lane 0's wait.
+              const int u = lane & 7;
+              const long long obase = static_cast<long long>(I.b) * p.o_batch +
+                                      static_cast<long long>(I.h - p.o_head_base) * p.o_head + 64 * rd + 8 * u;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int r = 4 * i + (lane >> 3);
+                const int grow = I.q0 + warp * 32 + r;
+                const uint4 val = ld_shared_v4u(wstage + r * 128u + ((u ^ (r & 7)) << 4));
+                if (grow < p.q_len) {
+                  char* dst = reinterpret_cast<char*>(p.o + obase + static_cast<long long>(grow) * p.o_tok);
+                  for (int pi = 0; pi < p.n_peers; ++pi)
+                    *reinterpret_cast<uint4*>(dst + p.peer_delta[pi]) = val;
+                }
+              }
+            }
           }
         }
         ++e;
@@ -457,11 +485,21 @@ __global__ void __launch_bounds__(kS3Threads, 1)
   }
 
   if (warp < 4 && lane == 0) tma_store_wait_all();  // the output stores have completed
+  if (peers_go && warp < 4) __threadfence_system();  // peer stores before the arrival below
   tc_fence_before();
   __syncthreads();
   if (warp == 4) {
     tc_fence_after();
     tmem_dealloc(tmem, kS3TmemCols);
+  }
+  if (peers_go && threadIdx.x == 0 && *abort_flag == 0) {
+    // This CTA's items are in every peer's output: count them on each peer's
+    // arrival word for this rank (a CTA that timed out does not arrive, so the
+    // peers' waits report the failure instead of reading a partial output).
+    const int mine = static_cast<int>(blockIdx.x) < p.n_items
+                         ? (p.n_items - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                         : 0;
+    for (int pi = 0; pi < p.n_peers; ++pi) red_add_release_sys(p.peer_arrive[pi], static_cast<unsigned>(mine));
   }
 #undef BAR
 }
@@ -469,8 +507,7 @@ __global__ void __launch_bounds__(kS3Threads, 1)
 }  // namespace
 
 // One query tile per work item (n_q_tiles = ceil(q_len / 128)); head dim 64
-// or 128, no score probe, legacy numerics, no peer stores (launch_attn_fwd
-// checks).
+// or 128, no score probe, legacy numerics (launch_attn_fwd checks).
 template <int HD>
 static cudaError_t launch_s3_hd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                 const AttnFwdParams& p, int heads_in_launch, int batch, int dev, int sms,
@@ -479,9 +516,10 @@ static cudaError_t launch_s3_hd(const CUtensorMap& tq, const CUtensorMap& tk, co
   cudaError_t e;
   const uint64_t bit = 1ull << (dev & 63);
   if ((configured.load(std::memory_order_acquire) & bit) == 0) {
-    e = cudaFuncSetAttribute(attn_s3_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             S3Smem<HD>::kBytes);
-    if (e != cudaSuccess) return e;
+    for (auto fn : {attn_s3_sm100_kernel<HD, false>, attn_s3_sm100_kernel<HD, true>}) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, S3Smem<HD>::kBytes);
+      if (e != cudaSuccess) return e;
+    }
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   AttnFwdParams q = p;
@@ -498,7 +536,8 @@ static cudaError_t launch_s3_hd(const CUtensorMap& tq, const CUtensorMap& tk, co
   if (ax_make_tmap(nullptr, &to, p.o, HD, p.q_len, p.head_offset + heads_in_launch - p.o_head_base, batch,
                    p.o_tok, p.o_head, p.o_batch, 32) != ANIMAXS_OK)
     return cudaErrorInvalidValue;
-  attn_s3_sm100_kernel<HD><<<grid, kS3Threads, S3Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
+  auto kernel = q.n_peers > 0 ? attn_s3_sm100_kernel<HD, true> : attn_s3_sm100_kernel<HD, false>;
+  kernel<<<grid, kS3Threads, S3Smem<HD>::kBytes, stream>>>(tq, tk, tv, to, q);
   return cudaGetLastError();
 }
 

@@ -94,8 +94,9 @@ cudaError_t launch_attn_wide(const CUtensorMap& tq, const CUtensorMap& tk, const
 
 int attn_fwd_rows_per_cta();  // query rows of a paired work item (head dims 64 / 128)
 // Work items launch_attn_fwd deals for head dims 64 / 128 (pairs of query
-// tiles, or single tiles when pairs would leave more than half of `sms` idle).
-long long attn_fwd_work_items(int q_len, int heads_in_launch, int batch, int sms);
+// tiles, or single tiles when pairs would leave more than half of `sms` idle,
+// or, for a launch with peer stores, any of them idle).
+long long attn_fwd_work_items(int q_len, int heads_in_launch, int batch, int sms, bool peers);
 
 cudaError_t launch_qk_norm(NormParams p, cudaStream_t stream);
 

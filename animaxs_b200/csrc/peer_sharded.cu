@@ -212,7 +212,7 @@ extern "C" int animaxs_attn_forward_head_sharded_peer(animaxs_attn_ctx* ctx, ani
   const int hr = d->heads / world;
   const int h0 = rank * hr;
   const unsigned int items =
-      static_cast<unsigned int>(ax::attn_fwd_work_items(d->q_len, hr, d->batch, ctx->num_sms));
+      static_cast<unsigned int>(ax::attn_fwd_work_items(d->q_len, hr, d->batch, ctx->num_sms, true));
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   DeviceGuard guard(ctx->device);
 
