@@ -237,6 +237,20 @@ def _peer_worker(rank, world, port, out):
     errs.append(float((got.float() - ref.float()).abs().max()))
     dist.barrier()
     ps.close()
+    # 4096 tokens: 8 heads x 16 pairs = 128 pairs per rank leave SMs idle, so
+    # the launch deals 256 single tiles -- more than one per CTA, the per-rank
+    # shape of 16K tokens over 8 ranks.  Two calls in a row.
+    ps = PeerShardedAttention(ex, rank, world, (1, 4096, 16, 128))
+    rope = torch.from_numpy(ax.DitRoPE.generate(1, 64, 64)).cuda()
+    for call in range(2):
+        q, k, v = (torch.randn(1, 4096, 16, 128, generator=g, device="cuda").half() for _ in range(3))
+        got = ps(q, k, v, qk_norm="rms_rope", rope_table=rope)
+        ex.synchronize()
+        ref = ex.attention(q, k, v, qk_norm="rms_rope", rope_table=rope)
+        torch.cuda.synchronize()
+        errs.append(float((got.float() - ref.float()).abs().max()))
+        dist.barrier()
+    ps.close()
     out[rank] = errs
     dist.barrier()
     dist.destroy_process_group()
@@ -250,13 +264,14 @@ def test_peer_fused_head_sharded_matches_single_gpu():
     """The attention kernel stores its heads into both ranks' outputs (NVLink);
     every rank's buffer equals the single-GPU result bit for bit: three calls
     in a row (token-major, norm + RoPE and plain), a head-major GQA causal
-    call with a ragged length, and head_dim 64 over two images."""
+    call with a ragged length, head_dim 64 over two images, and two calls at
+    4096 tokens whose 256 single-tile items are more than one per CTA."""
     import torch.multiprocessing as mp
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     for rank in (0, 1):
-        assert out[rank] == [0.0] * 5, f"rank {rank}: max differences {out[rank]}"
+        assert out[rank] == [0.0] * 7, f"rank {rank}: max differences {out[rank]}"
 
 
 def _peer_absent_worker(rank, world, port, out, one_gpu=False):
